@@ -1,0 +1,386 @@
+// bindings.cpp - the `_flash_attn_metal` Python module over the C ABI in
+// fa_b200.h. Keeps the reference module's surface (python/bindings.cpp:239-269):
+//   initialize() -> bool
+//   load_shaders(metallib_path) -> bool      accepted no-op (kernels are built ahead of time)
+//   compile_shaders(shader_source) -> bool   accepted no-op
+//   get_device_info() -> {device_name, max_buffer_length, initialized}
+//   forward(Q, K, V, softmax_scale=0.0, is_causal=False, dropout_p=0.0,
+//           alibi_slopes=None, window_size=None, cos=None, sin=None)
+// with the reference's error behaviour: initialize/load/compile print to
+// stderr and return False; forward raises RuntimeError("Forward pass error: ...").
+//
+// forward takes NumPy arrays (float16, float32, ml_dtypes.bfloat16; the host
+// path copies to and from the device like FlashAttentionForward::execute) or
+// torch tensors (CUDA tensors run zero-copy on the current stream; CPU
+// tensors take the host path). Keyword-only extras: out_dtype, rope_theta,
+// return_lse.
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cstring>
+#include <iostream>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/fa_b200.h"
+
+namespace py = pybind11;
+
+namespace {
+
+int g_device = 0;
+
+std::string err_text(fa_status st) {
+  std::string s = fa_last_error();
+  if (s.empty()) s = "status " + std::to_string((int)st);
+  return s;
+}
+
+[[noreturn]] void forward_error(const std::string& what) {
+  throw std::runtime_error("Forward pass error: " + what);
+}
+
+bool is_torch_tensor(const py::object& o) {
+  return py::hasattr(o, "data_ptr") && py::hasattr(o, "is_cuda") && py::hasattr(o, "stride");
+}
+
+int dtype_code_from_name(const std::string& n) {
+  if (n == "float16" || n == "torch.float16" || n == "torch.half") return FA_F16;
+  if (n == "bfloat16" || n == "torch.bfloat16") return FA_BF16;
+  if (n == "float32" || n == "torch.float32" || n == "torch.float") return FA_F32;
+  return -1;
+}
+
+int parse_out_dtype(const py::object& od) {
+  if (od.is_none()) return -1;
+  const std::string n = py::str(od);
+  const int c = dtype_code_from_name(n);
+  if (c < 0) forward_error("out_dtype must be float16, bfloat16 or float32");
+  return c;
+}
+
+void fill_params(fa_params& p, const std::vector<int64_t>& qs, const std::vector<int64_t>& ks,
+                 float scale, bool causal, float dropout_p, const py::object& alibi,
+                 const py::object& window, bool rotary, float rope_theta) {
+  fa_params_init(&p);
+  p.batch_size = (uint32_t)qs[0];
+  p.seqlen_q = (uint32_t)qs[1];
+  p.num_heads_q = (uint32_t)qs[2];
+  p.head_dim = (uint32_t)qs[3];
+  p.seqlen_k = (uint32_t)ks[1];
+  p.num_heads_k = (uint32_t)ks[2];
+  p.softmax_scale = scale;
+  p.is_causal = causal ? 1 : 0;
+  p.dropout_p = dropout_p;
+  if (!window.is_none()) {
+    py::tuple ws = window.cast<py::tuple>();
+    if (py::len(ws) == 2) {
+      p.window_left = ws[0].cast<int>();
+      p.window_right = ws[1].cast<int>();
+    }
+  }
+  p.has_alibi = alibi.is_none() ? 0 : 1;
+  p.has_rotary = rotary ? 1 : 0;
+  p.rope_theta = rope_theta;
+}
+
+void check_shapes(const std::vector<int64_t>& qs, const std::vector<int64_t>& ks,
+                  const std::vector<int64_t>& vs) {
+  if (qs.size() != 4 || ks.size() != 4 || vs.size() != 4)
+    forward_error("Input arrays must be 4D [batch, seqlen, num_heads, head_dim]");
+  if (ks[0] != qs[0] || vs[0] != qs[0] || vs[1] != ks[1] || vs[2] != ks[2] || ks[3] != qs[3] ||
+      vs[3] != qs[3])
+    forward_error("K and V shapes must match");
+}
+
+// ------------------------------------------------------------------ numpy
+py::object bf16_numpy_dtype() { return py::module_::import("ml_dtypes").attr("bfloat16"); }
+
+int numpy_code(const py::array& a) {
+  const std::string n = py::str(a.dtype());
+  return dtype_code_from_name(n);
+}
+
+py::dtype numpy_dtype_of(int code) {
+  if (code == FA_F16) return py::dtype("float16");
+  if (code == FA_F32) return py::dtype("float32");
+  return py::dtype::from_args(bf16_numpy_dtype());
+}
+
+py::object forward_numpy(py::object Q, py::object K, py::object V, float scale, bool causal,
+                         float dropout_p, py::object alibi, py::object window, py::object cos,
+                         py::object sin, int out_code, float rope_theta, bool return_lse) {
+  py::module_ np = py::module_::import("numpy");
+  py::array q = np.attr("ascontiguousarray")(Q);
+  py::array k = np.attr("ascontiguousarray")(K);
+  py::array v = np.attr("ascontiguousarray")(V);
+  const int code = numpy_code(q);
+  if (code < 0 || numpy_code(k) != code || numpy_code(v) != code)
+    forward_error("Input arrays must be float16, bfloat16 or float32, all of one dtype");
+  std::vector<int64_t> qs(q.shape(), q.shape() + q.ndim()), ks(k.shape(), k.shape() + k.ndim()),
+      vs(v.shape(), v.shape() + v.ndim());
+  check_shapes(qs, ks, vs);
+  const bool rotary_tables = !cos.is_none() && !sin.is_none();
+  const bool rotary = rotary_tables || rope_theta > 0.f;
+  fa_params p;
+  fill_params(p, qs, ks, scale, causal, dropout_p, alibi, window, rotary, rope_theta);
+  p.dtype = code;
+  p.out_dtype = out_code;
+  const int oc = out_code < 0 ? code : out_code;
+  py::array c_arr, s_arr;
+  const float* cp = nullptr;
+  const float* sp = nullptr;
+  if (rotary_tables) {
+    c_arr = np.attr("ascontiguousarray")(cos, "float32");
+    s_arr = np.attr("ascontiguousarray")(sin, "float32");
+    const int64_t need = std::max(qs[1], ks[1]) * (qs[3] / 2);
+    if (c_arr.size() < need || s_arr.size() < need)
+      forward_error("cos/sin tables must hold [max(seqlen_q, seqlen_k), head_dim/2] float32 values");
+    cp = static_cast<const float*>(c_arr.data());
+    sp = static_cast<const float*>(s_arr.data());
+  }
+  py::array out(numpy_dtype_of(oc), std::vector<py::ssize_t>{(py::ssize_t)qs[0], (py::ssize_t)qs[1],
+                                                              (py::ssize_t)qs[2], (py::ssize_t)qs[3]});
+  py::array_t<float> lse;
+  float* lp = nullptr;
+  if (return_lse) {
+    lse = py::array_t<float>(std::vector<py::ssize_t>{(py::ssize_t)qs[0], (py::ssize_t)qs[2], (py::ssize_t)qs[1]});
+    lp = lse.mutable_data();
+  }
+  fa_status st;
+  {
+    py::gil_scoped_release nogil;
+    st = fa_forward_host(&p, q.data(), k.data(), v.data(), out.mutable_data(), lp, cp, sp);
+  }
+  if (st != FA_OK) forward_error(err_text(st));
+  if (return_lse) return py::make_tuple(out, lse);
+  return out;
+}
+
+// ------------------------------------------------------------------ torch
+std::vector<int64_t> tsize(const py::object& t) { return t.attr("shape").cast<std::vector<int64_t>>(); }
+std::vector<int64_t> tstride(const py::object& t) { return t.attr("stride")().cast<std::vector<int64_t>>(); }
+
+py::object torch_dtype_of(int code) {
+  py::module_ torch = py::module_::import("torch");
+  if (code == FA_F16) return torch.attr("float16");
+  if (code == FA_BF16) return torch.attr("bfloat16");
+  return torch.attr("float32");
+}
+
+// Innermost stride 1 (else a contiguous copy); returns the possibly-new tensor.
+py::object inner_contig(py::object t) {
+  auto st = tstride(t);
+  if (st.size() == 4 && st[3] == 1) return t;
+  return t.attr("contiguous")();
+}
+
+// A caller-provided output tensor must match shape, dtype and device and be contiguous.
+py::object check_out(py::object out, const py::tuple& shape, int oc, bool cuda) {
+  py::module_ torch = py::module_::import("torch");
+  if (tsize(out) != shape.cast<std::vector<int64_t>>()) forward_error("out has the wrong shape");
+  if (dtype_code_from_name(py::str(out.attr("dtype"))) != oc) forward_error("out has the wrong dtype");
+  if (out.attr("is_cuda").cast<bool>() != cuda) forward_error("out is on the wrong device");
+  if (!out.attr("is_contiguous")().cast<bool>()) forward_error("out must be contiguous");
+  return out;
+}
+
+py::object forward_torch(py::object Q, py::object K, py::object V, float scale, bool causal,
+                         float dropout_p, py::object alibi, py::object window, py::object cos,
+                         py::object sin, int out_code, float rope_theta, bool return_lse,
+                         py::object out_arg) {
+  py::module_ torch = py::module_::import("torch");
+  const bool cuda = Q.attr("is_cuda").cast<bool>();
+  if (K.attr("is_cuda").cast<bool>() != cuda || V.attr("is_cuda").cast<bool>() != cuda)
+    forward_error("Q, K and V must all be CUDA tensors or all CPU tensors");
+  const int code = dtype_code_from_name(py::str(Q.attr("dtype")));
+  if (code < 0 || dtype_code_from_name(py::str(K.attr("dtype"))) != code ||
+      dtype_code_from_name(py::str(V.attr("dtype"))) != code)
+    forward_error("Input tensors must be float16, bfloat16 or float32, all of one dtype");
+  std::vector<int64_t> qs = tsize(Q), ks = tsize(K), vs = tsize(V);
+  check_shapes(qs, ks, vs);
+  const bool rotary_tables = !cos.is_none() && !sin.is_none();
+  const bool rotary = rotary_tables || rope_theta > 0.f;
+  fa_params p;
+  fill_params(p, qs, ks, scale, causal, dropout_p, alibi, window, rotary, rope_theta);
+  p.dtype = code;
+  p.out_dtype = out_code;
+  const int oc = out_code < 0 ? code : out_code;
+  py::tuple shape = py::make_tuple(qs[0], qs[1], qs[2], qs[3]);
+
+  if (!cuda) {
+    // CPU tensors: host path (contiguous), like the NumPy route.
+    py::object q = Q.attr("contiguous")(), k = K.attr("contiguous")(), v = V.attr("contiguous")();
+    py::object out = out_arg.is_none() ? torch.attr("empty")(shape, py::arg("dtype") = torch_dtype_of(oc))
+                                       : check_out(out_arg, shape, oc, false);
+    py::object lse = py::none();
+    float* lp = nullptr;
+    if (return_lse) {
+      lse = torch.attr("empty")(py::make_tuple(qs[0], qs[2], qs[1]), py::arg("dtype") = torch.attr("float32"));
+      lp = reinterpret_cast<float*>(lse.attr("data_ptr")().cast<uintptr_t>());
+    }
+    py::object ct = py::none(), stt = py::none();
+    const float* cp = nullptr;
+    const float* sp = nullptr;
+    if (rotary_tables) {
+      ct = torch.attr("as_tensor")(cos, py::arg("dtype") = torch.attr("float32")).attr("contiguous")();
+      stt = torch.attr("as_tensor")(sin, py::arg("dtype") = torch.attr("float32")).attr("contiguous")();
+      cp = reinterpret_cast<const float*>(ct.attr("data_ptr")().cast<uintptr_t>());
+      sp = reinterpret_cast<const float*>(stt.attr("data_ptr")().cast<uintptr_t>());
+    }
+    const void* qp = reinterpret_cast<const void*>(q.attr("data_ptr")().cast<uintptr_t>());
+    const void* kp = reinterpret_cast<const void*>(k.attr("data_ptr")().cast<uintptr_t>());
+    const void* vp = reinterpret_cast<const void*>(v.attr("data_ptr")().cast<uintptr_t>());
+    void* op = reinterpret_cast<void*>(out.attr("data_ptr")().cast<uintptr_t>());
+    fa_status st;
+    {
+      py::gil_scoped_release nogil;
+      st = fa_forward_host(&p, qp, kp, vp, op, lp, cp, sp);
+    }
+    if (st != FA_OK) forward_error(err_text(st));
+    if (return_lse) return py::make_tuple(out, lse);
+    return out;
+  }
+
+  py::object dev = Q.attr("device");
+  const int dev_index = dev.attr("index").is_none() ? 0 : dev.attr("index").cast<int>();
+  fa_status st = fa_init(dev_index);
+  if (st != FA_OK) forward_error(err_text(st));
+  py::object q = inner_contig(Q), k = inner_contig(K), v = inner_contig(V);
+  auto qst = tstride(q), kst = tstride(k), vst = tstride(v);
+  for (int i = 0; i < 3; ++i) {
+    p.q_stride[i] = qst[i];
+    p.k_stride[i] = kst[i];
+    p.v_stride[i] = vst[i];
+  }
+  py::object out = out_arg.is_none()
+                       ? torch.attr("empty")(shape, py::arg("dtype") = torch_dtype_of(oc), py::arg("device") = dev)
+                       : check_out(out_arg, shape, oc, true);
+  py::object lse = py::none();
+  float* lp = nullptr;
+  if (return_lse) {
+    lse = torch.attr("empty")(py::make_tuple(qs[0], qs[2], qs[1]), py::arg("dtype") = torch.attr("float32"),
+                              py::arg("device") = dev);
+    lp = reinterpret_cast<float*>(lse.attr("data_ptr")().cast<uintptr_t>());
+  }
+  py::object ct = py::none(), stt = py::none();
+  const float* cp = nullptr;
+  const float* sp = nullptr;
+  if (rotary_tables) {
+    ct = torch.attr("as_tensor")(cos, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    stt = torch.attr("as_tensor")(sin, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    const int64_t need = std::max(qs[1], ks[1]) * (qs[3] / 2);
+    if (ct.attr("numel")().cast<int64_t>() < need || stt.attr("numel")().cast<int64_t>() < need)
+      forward_error("cos/sin tables must hold [max(seqlen_q, seqlen_k), head_dim/2] float32 values");
+    cp = reinterpret_cast<const float*>(ct.attr("data_ptr")().cast<uintptr_t>());
+    sp = reinterpret_cast<const float*>(stt.attr("data_ptr")().cast<uintptr_t>());
+  }
+  void* stream = reinterpret_cast<void*>(
+      torch.attr("cuda").attr("current_stream")(dev).attr("cuda_stream").cast<uintptr_t>());
+  const void* qp = reinterpret_cast<const void*>(q.attr("data_ptr")().cast<uintptr_t>());
+  const void* kp = reinterpret_cast<const void*>(k.attr("data_ptr")().cast<uintptr_t>());
+  const void* vp = reinterpret_cast<const void*>(v.attr("data_ptr")().cast<uintptr_t>());
+  void* op = reinterpret_cast<void*>(out.attr("data_ptr")().cast<uintptr_t>());
+  st = fa_forward(&p, qp, kp, vp, op, lp, cp, sp, nullptr, 0, stream);
+  if (st != FA_OK) forward_error(err_text(st));
+  if (return_lse) return py::make_tuple(out, lse);
+  return out;
+}
+
+// ------------------------------------------------------------ module API
+bool py_initialize() {
+  fa_status st = fa_init(g_device);
+  if (st != FA_OK) {
+    std::cerr << "Initialization error: " << err_text(st) << "\n";
+    return false;
+  }
+  return true;
+}
+
+bool py_load_shaders(const std::string& /*metallib_path*/) {
+  // Kernels are compiled ahead of time for sm_100a; there is nothing to load.
+  return py_initialize();
+}
+
+bool py_compile_shaders(const std::string& /*shader_source*/) {
+  // Accepted no-op: the CUDA kernels are compiled when the library is built.
+  return py_initialize();
+}
+
+py::dict py_get_device_info() {
+  py::dict info;
+  char name[256] = {0};
+  uint64_t mem = 0;
+  int init = 0;
+  fa_status st = fa_device_info(g_device, name, sizeof(name), &mem, &init);
+  if (st != FA_OK && st != FA_ERR_NO_DEVICE) {
+    std::cerr << "Device info error: " << err_text(st) << "\n";
+    return py::dict();
+  }
+  info["device_name"] = std::string(name);
+  info["max_buffer_length"] = mem;
+  info["initialized"] = init != 0;
+  return info;
+}
+
+py::object py_forward(py::object Q, py::object K, py::object V, float softmax_scale, bool is_causal,
+                      float dropout_p, py::object alibi_slopes, py::object window_size, py::object cos,
+                      py::object sin, py::object out_dtype, py::object rope_theta, bool return_lse,
+                      py::object out) {
+  const int oc = parse_out_dtype(out_dtype);
+  const float theta = rope_theta.is_none() ? 0.f : rope_theta.cast<float>();
+  if (is_torch_tensor(Q))
+    return forward_torch(Q, K, V, softmax_scale, is_causal, dropout_p, alibi_slopes, window_size, cos,
+                         sin, oc, theta, return_lse, out);
+  if (!out.is_none()) forward_error("out= is supported for torch tensors only");
+  return forward_numpy(Q, K, V, softmax_scale, is_causal, dropout_p, alibi_slopes, window_size, cos, sin,
+                       oc, theta, return_lse);
+}
+
+void py_check_status() {
+  fa_status st = fa_check_device_status();
+  if (st != FA_OK) throw std::runtime_error("Device status error: " + err_text(st));
+}
+
+py::tuple py_pool_stats() {
+  uint64_t h = 0, m = 0, b = 0;
+  fa_status st = fa_pool_stats(&h, &m, &b);
+  if (st != FA_OK) throw std::runtime_error(err_text(st));
+  return py::make_tuple(h, m, b);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_flash_attn_metal, m) {
+  m.doc() = "FlashAttention-2 forward for NVIDIA B200 (sm_100a), drop-in for the Metal module";
+  m.def("initialize", &py_initialize, "Initialize the CUDA device");
+  m.def("load_shaders", &py_load_shaders, py::arg("metallib_path"),
+        "Accepted for compatibility; kernels are compiled ahead of time");
+  m.def("compile_shaders", &py_compile_shaders, py::arg("shader_source"),
+        "Accepted for compatibility; kernels are compiled ahead of time");
+  m.def("get_device_info", &py_get_device_info, "Get CUDA device information");
+  m.def("forward", &py_forward, py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("softmax_scale") = 0.0f,
+        py::arg("is_causal") = false, py::arg("dropout_p") = 0.0f, py::arg("alibi_slopes") = py::none(),
+        py::arg("window_size") = py::none(), py::arg("cos") = py::none(), py::arg("sin") = py::none(),
+        py::kw_only(), py::arg("out_dtype") = py::none(), py::arg("rope_theta") = py::none(),
+        py::arg("return_lse") = false, py::arg("out") = py::none(), "Flash Attention forward pass");
+  m.def("check_status", &py_check_status,
+        "Raise if a kernel recorded a timeout or range error since the last check");
+  m.def("launch_count", []() { return fa_launch_count(); },
+        "Number of kernels this library launched on the calling thread");
+  m.def("kernel_timing_enable", []() { fa_kernel_timing_enable(); },
+        "Time every attention-kernel launch of this thread with CUDA events");
+  m.def("kernel_timing_read", []() {
+    double ms = 0;
+    uint64_t n = 0;
+    fa_status st = fa_kernel_timing_read(&ms, &n);
+    if (st != FA_OK) throw std::runtime_error(err_text(st));
+    return py::make_tuple(ms, n);
+  }, "(summed ms, launches) of the attention kernel since kernel_timing_enable; disables timing");
+  m.def("pool_stats", &py_pool_stats, "(hits, misses, bytes reserved) of the device buffer pool");
+  m.def("pool_clear", []() {
+    fa_status st = fa_pool_clear();
+    if (st != FA_OK) throw std::runtime_error(err_text(st));
+  });
+}

@@ -1,0 +1,729 @@
+// fa_api.cu - host side of the library: the C ABI declared in fa_b200.h.
+//
+// Replaces the reference's host runtime (src/flash_attn_core.cpp): device
+// set-up (MetalDevice::initialize, :50-64), the power-of-two buffer pool
+// (BufferPool, :193-246), and FlashAttentionForward::execute (:276-407),
+// whose steps are kept in the same order for the host-pointer entry point:
+// size buffers, take them from the pool, copy Q/K/V in, bind tables,
+// dispatch, wait, copy O (and LSE) out, return buffers to the pool.
+//
+// Dispatch: fp16/bf16 with head_dim 64 or 128 and 16-byte aligned rows run
+// on the tcgen05 kernel (fa_fwd_sm100.cu); everything else (fp32 inputs,
+// other head dims) runs on the CUDA-core kernel (fa_fwd_simt.cu). There is
+// no CPU path: without a CUDA device every entry point returns an error.
+#include "../../include/fa_b200.h"
+#include "fa_internal.h"
+#include "fa_ptx.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace fa {
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local uint64_t g_launches = 0;
+// Attention-kernel timing (fa_kernel_timing_enable / _read).
+thread_local bool g_timing = false;
+thread_local std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events;
+
+fa_status fail(fa_status st, const std::string& msg) {
+  g_last_error = msg;
+  return st;
+}
+
+fa_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(FA_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define FA_CUDA(call)                                        \
+  do {                                                       \
+    cudaError_t e_ = (call);                                 \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);      \
+  } while (0)
+
+size_t dtype_size(int dt) { return dt == kF32 ? 4 : 2; }
+
+// Power-of-two size-bucketed cache of device buffers (the reference's
+// BufferPool, src/flash_attn_core.cpp:199-234), one per device.
+class DevicePool {
+ public:
+  void* get(size_t bytes) {
+    size_t rounded = 256;
+    while (rounded < bytes) rounded <<= 1;
+    std::lock_guard<std::mutex> g(mu_);
+    auto it = free_.find(rounded);
+    if (it != free_.end() && !it->second.empty()) {
+      void* p = it->second.back();
+      it->second.pop_back();
+      ++hits_;
+      return p;
+    }
+    void* p = nullptr;
+    if (cudaMalloc(&p, rounded) != cudaSuccess) {
+      cudaGetLastError();
+      // Free everything cached and retry once before giving up.
+      release_locked();
+      if (cudaMalloc(&p, rounded) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+      }
+    }
+    size_of_[p] = rounded;
+    reserved_ += rounded;
+    ++misses_;
+    return p;
+  }
+  void put(void* p) {
+    if (!p) return;
+    std::lock_guard<std::mutex> g(mu_);
+    free_[size_of_[p]].push_back(p);
+  }
+  void clear() {
+    std::lock_guard<std::mutex> g(mu_);
+    release_locked();
+    hits_ = misses_ = 0;
+  }
+  void stats(uint64_t* h, uint64_t* m, uint64_t* b) {
+    std::lock_guard<std::mutex> g(mu_);
+    if (h) *h = hits_;
+    if (m) *m = misses_;
+    if (b) *b = reserved_;
+  }
+
+ private:
+  void release_locked() {
+    for (auto& kv : free_)
+      for (void* p : kv.second) {
+        cudaFree(p);
+        reserved_ -= size_of_[p];
+        size_of_.erase(p);
+      }
+    free_.clear();
+  }
+  std::mutex mu_;
+  std::map<size_t, std::vector<void*>> free_;
+  std::map<void*, size_t> size_of_;
+  uint64_t hits_ = 0, misses_ = 0, reserved_ = 0;
+};
+
+// RAII lease of a pool buffer.
+struct Lease {
+  DevicePool* pool = nullptr;
+  void* p = nullptr;
+  Lease() = default;
+  Lease(DevicePool* pl, size_t bytes) : pool(pl), p(bytes ? pl->get(bytes) : nullptr) {}
+  Lease(const Lease&) = delete;
+  Lease& operator=(const Lease&) = delete;
+  ~Lease() {
+    if (pool && p) pool->put(p);
+  }
+};
+
+struct DeviceState {
+  int device = -1;
+  bool ready = false;
+  unsigned* status = nullptr;       // in-kernel status word
+  cudaStream_t host_stream = nullptr;
+  DevicePool pool;
+  std::mutex mu;                    // serialises the host-pointer path and the caches
+  // RoPE table cache: (theta bits, D) -> tables with `rows` rows.
+  struct Rope {
+    float theta = 0.f;
+    int D = 0, rows = 0;
+    float* cs = nullptr;
+    float* sn = nullptr;
+  } rope;
+  // Stream-ordered workspaces for fa_forward calls without a workspace.
+  std::map<cudaStream_t, std::pair<void*, size_t>> ws;
+};
+
+std::mutex g_devices_mu;
+std::map<int, std::unique_ptr<DeviceState>> g_devices;
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+fa_status get_encode() {
+  if (g_encode) return FA_OK;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                                   cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return fail(FA_ERR_CUDA, "cuTensorMapEncodeTiled entry point not available");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return FA_OK;
+}
+
+fa_status device_state(DeviceState** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  }
+  std::lock_guard<std::mutex> g(g_devices_mu);
+  auto& slot = g_devices[dev];
+  if (!slot) slot.reset(new DeviceState());
+  DeviceState* ds = slot.get();
+  if (!ds->ready) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+      cudaGetLastError();
+      return fail(FA_ERR_NO_DEVICE, "no CUDA device visible");
+    }
+    cudaDeviceProp prop;
+    FA_CUDA(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+      return fail(FA_ERR_UNSUPPORTED, std::string("device '") + prop.name +
+                                          "' is not sm_100 (B200); this library is built for sm_100a only");
+    FA_CUDA(cudaMalloc(&ds->status, sizeof(unsigned)));
+    FA_CUDA(cudaMemset(ds->status, 0, sizeof(unsigned)));
+    FA_CUDA(cudaStreamCreateWithFlags(&ds->host_stream, cudaStreamNonBlocking));
+    ds->device = dev;
+    ds->ready = true;
+  }
+  *out = ds;
+  return FA_OK;
+}
+
+// ---------------------------------------------------------------- validation
+struct Plan {
+  AttnArgs a;
+  int dtype, out_dtype;
+  bool tc;          // tensor-core path
+  bool rope;
+  bool need_q16, need_k16, need_v16;   // operands staged as fp16 in the workspace
+  float rope_theta;
+  size_t ws_bytes;
+};
+
+void default_strides(const int64_t in[3], int64_t out[3], int64_t S, int64_t H, int64_t D) {
+  if (in[0] == 0 && in[1] == 0 && in[2] == 0) {
+    out[0] = S * H * D;
+    out[1] = H * D;
+    out[2] = D;
+  } else {
+    out[0] = in[0];
+    out[1] = in[1];
+    out[2] = in[2];
+  }
+}
+
+fa_status make_plan(const fa_params* p, Plan* pl) {
+  if (!p) return fail(FA_ERR_INVALID_ARG, "params is NULL");
+  if (p->dtype < 0 || p->dtype > 2) return fail(FA_ERR_INVALID_ARG, "dtype must be 0 (f16), 1 (bf16) or 2 (f32)");
+  const int out_dt = p->out_dtype < 0 ? p->dtype : p->out_dtype;
+  if (out_dt > 2) return fail(FA_ERR_INVALID_ARG, "out_dtype must be -1, 0, 1 or 2");
+  if (p->dropout_p != 0.f)
+    return fail(FA_ERR_UNSUPPORTED, "dropout_p != 0 is not supported (the reference kernel ignores it)");
+  if (p->has_alibi) return fail(FA_ERR_UNSUPPORTED, "alibi_slopes are not supported (the reference kernel ignores them)");
+  if (p->window_left != -1 || p->window_right != -1)
+    return fail(FA_ERR_UNSUPPORTED, "window_size is not supported (the reference kernel ignores it)");
+  if (p->head_dim == 0 || p->head_dim > 256)
+    return fail(FA_ERR_UNSUPPORTED, "head_dim must be in [1, 256]");
+  if (p->num_heads_k == 0 || p->num_heads_q % p->num_heads_k != 0)
+    return fail(FA_ERR_INVALID_ARG, "num_heads_q must be a positive multiple of num_heads_k");
+  const uint32_t group = p->num_heads_q / p->num_heads_k;
+  if (p->gqa_group_size != 0 && p->gqa_group_size != group)
+    return fail(FA_ERR_INVALID_ARG, "gqa_group_size must equal num_heads_q / num_heads_k");
+  const uint64_t lim = (1ull << 31) - 1;
+  if (p->batch_size > 65535 || p->seqlen_q > lim || p->seqlen_k > lim || p->num_heads_q > 65535)
+    return fail(FA_ERR_INVALID_ARG, "tensor dimensions out of range");
+  if (!std::isfinite(p->softmax_scale)) return fail(FA_ERR_INVALID_ARG, "softmax_scale must be finite");
+
+  AttnArgs& a = pl->a;
+  std::memset(&a, 0, sizeof(a));
+  a.B = (int)p->batch_size;
+  a.Sq = (int)p->seqlen_q;
+  a.Sk = (int)p->seqlen_k;
+  a.Hq = (int)p->num_heads_q;
+  a.Hk = (int)p->num_heads_k;
+  a.D = (int)p->head_dim;
+  a.group = (int)group;
+  a.scale = p->softmax_scale;
+  a.scale_log2 = (float)((double)p->softmax_scale * 1.4426950408889634);
+  a.causal = p->is_causal ? 1 : 0;
+  a.q_begin = 0;
+  a.q_end = a.Sq;
+  a.kv_begin = 0;
+  a.kv_end = a.Sk;
+  int64_t qs[3], ks[3], vs[3], os[3];
+  default_strides(p->q_stride, qs, a.Sq, a.Hq, a.D);
+  default_strides(p->k_stride, ks, a.Sk, a.Hk, a.D);
+  default_strides(p->v_stride, vs, a.Sk, a.Hk, a.D);
+  default_strides(p->o_stride, os, a.Sq, a.Hq, a.D);
+  a.q_sb = qs[0]; a.q_ss = qs[1]; a.q_sh = qs[2];
+  a.k_sb = ks[0]; a.k_ss = ks[1]; a.k_sh = ks[2];
+  a.v_sb = vs[0]; a.v_ss = vs[1]; a.v_sh = vs[2];
+  a.o_sb = os[0]; a.o_ss = os[1]; a.o_sh = os[2];
+  for (int i = 0; i < 3; ++i)
+    if (qs[i] < 0 || ks[i] < 0 || vs[i] < 0 || os[i] < 0)
+      return fail(FA_ERR_INVALID_ARG, "strides must be non-negative");
+
+  pl->dtype = p->dtype;
+  pl->out_dtype = out_dt;
+  pl->rope = p->has_rotary != 0;
+  pl->rope_theta = p->rope_theta;
+  const int D = a.D;
+  auto al = [](int64_t s, int64_t mult) { return s % mult == 0; };
+  const int64_t in_mult = 16 / (int64_t)dtype_size(p->dtype);
+  const int64_t out_mult = 16 / (int64_t)dtype_size(out_dt);
+  bool strides_ok = true;
+  for (int i = 0; i < 3; ++i)
+    strides_ok &= al(qs[i], in_mult) && al(ks[i], in_mult) && al(vs[i], in_mult) && al(os[i], out_mult);
+  pl->tc = (p->dtype == kF16 || p->dtype == kBF16) && (D == 64 || D == 128) && strides_ok;
+  pl->need_q16 = pl->tc && pl->rope;
+  pl->need_k16 = pl->tc && pl->rope;
+  pl->need_v16 = pl->tc && p->dtype == kBF16;
+  size_t ws = 0;
+  auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+  if (pl->need_q16) ws += up((size_t)a.B * a.Sq * a.Hq * D * 2);
+  if (pl->need_k16) ws += up((size_t)a.B * a.Sk * a.Hk * D * 2);
+  if (pl->need_v16) ws += up((size_t)a.B * a.Sk * a.Hk * D * 2);
+  pl->ws_bytes = ws;
+  return FA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+fa_status encode_map(CUtensorMap* m, const void* base, bool bf16, int D, int H, int S, int B,
+                     int64_t sb, int64_t ss, int64_t sh) {
+  fa_status st = get_encode();
+  if (st != FA_OK) return st;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)ss * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, 1, 128, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                        const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FA_ERR_INVALID_ARG, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
+  return FA_OK;
+}
+
+// Cached RoPE tables from theta with at least `rows` rows.
+fa_status rope_from_theta(DeviceState* ds, float theta, int D, int rows, cudaStream_t stream,
+                          const float** cs, const float** sn) {
+  std::lock_guard<std::mutex> g(ds->mu);
+  auto& r = ds->rope;
+  if (!(r.cs && r.theta == theta && r.D == D && r.rows >= rows)) {
+    if (r.cs) {
+      FA_CUDA(cudaStreamSynchronize(stream));
+      cudaFree(r.cs);
+      cudaFree(r.sn);
+      r.cs = r.sn = nullptr;
+    }
+    const size_t bytes = (size_t)rows * (D / 2) * sizeof(float) + 16;
+    FA_CUDA(cudaMalloc(&r.cs, bytes));
+    FA_CUDA(cudaMalloc(&r.sn, bytes));
+    FA_CUDA(launch_rope_table(r.cs, r.sn, rows, D, (double)theta, stream));
+    r.theta = theta;
+    r.D = D;
+    r.rows = rows;
+  }
+  *cs = r.cs;
+  *sn = r.sn;
+  return FA_OK;
+}
+
+fa_status stream_workspace(DeviceState* ds, cudaStream_t stream, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> g(ds->mu);
+  auto& w = ds->ws[stream];
+  if (w.second < bytes) {
+    if (w.first) {
+      FA_CUDA(cudaStreamSynchronize(stream));
+      cudaFree(w.first);
+      w.first = nullptr;
+      w.second = 0;
+    }
+    FA_CUDA(cudaMalloc(&w.first, bytes));
+    w.second = bytes;
+  }
+  *out = w.first;
+  return FA_OK;
+}
+
+// Core of fa_forward / fa_forward_partial once the plan is fixed.
+fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float* cos,
+              const float* sin, void* workspace, size_t ws_bytes, cudaStream_t stream,
+              DeviceState* ds) {
+  AttnArgs& a = pl.a;
+  a.status = ds->status;
+  if (a.q_end <= a.q_begin || a.B == 0 || a.Hq == 0) return FA_OK;
+  if (!a.o) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
+  // No key at all (Sk == 0 or an empty split): O = 0, LSE = -inf.
+  if (a.kv_end <= a.kv_begin) {
+    cudaError_t e = launch_fill_empty(a, pl.out_dtype, stream);
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "fill_empty");
+  }
+  if (!q || !k || !v) return fail(FA_ERR_INVALID_ARG, "NULL tensor pointer");
+  const float* cs = cos;
+  const float* sn = sin;
+  if (pl.rope && (cs == nullptr || sn == nullptr)) {
+    if (!(pl.rope_theta > 0.f) || !std::isfinite(pl.rope_theta))
+      return fail(FA_ERR_INVALID_ARG, "has_rotary needs cos/sin tables or rope_theta > 0");
+    if (a.D % 2 != 0) return fail(FA_ERR_UNSUPPORTED, "RoPE from rope_theta needs an even head_dim");
+    fa_status st = rope_from_theta(ds, pl.rope_theta, a.D, a.Sq > a.Sk ? a.Sq : a.Sk, stream, &cs, &sn);
+    if (st != FA_OK) return st;
+  }
+  if (!pl.rope) cs = sn = nullptr;
+
+  if (!pl.tc) {
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.rope_cos = cs;
+    a.rope_sin = sn;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    if (g_timing) {
+      FA_CUDA(cudaEventCreate(&ev0));
+      FA_CUDA(cudaEventCreate(&ev1));
+      FA_CUDA(cudaEventRecord(ev0, stream));
+    }
+    cudaError_t e = launch_attn_simt(a, pl.dtype, pl.out_dtype, stream);
+    if (g_timing) {
+      FA_CUDA(cudaEventRecord(ev1, stream));
+      g_events.emplace_back(ev0, ev1);
+    }
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (CUDA-core kernel)");
+  }
+
+  // Tensor-core path.
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(a.o))
+    return fail(FA_ERR_INVALID_ARG, "tensor base addresses must be 16-byte aligned");
+  if (pl.ws_bytes > 0) {
+    if (workspace == nullptr) {
+      fa_status st = stream_workspace(ds, stream, pl.ws_bytes, &workspace);
+      if (st != FA_OK) return st;
+    } else if (ws_bytes < pl.ws_bytes) {
+      return fail(FA_ERR_INVALID_ARG, "workspace smaller than fa_workspace_size()");
+    } else if (!aligned16(workspace)) {
+      return fail(FA_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
+    }
+  }
+  uint8_t* wp = static_cast<uint8_t*>(workspace);
+  auto take = [&](size_t bytes) {
+    uint8_t* r = wp;
+    wp += (bytes + 255) & ~size_t(255);
+    return reinterpret_cast<__half*>(r);
+  };
+  const void* qs = q;
+  const void* ks = k;
+  const void* vs = v;
+  int64_t q_sb = a.q_sb, q_ss = a.q_ss, q_sh = a.q_sh;
+  int64_t k_sb = a.k_sb, k_ss = a.k_ss, k_sh = a.k_sh;
+  int64_t v_sb = a.v_sb, v_ss = a.v_ss, v_sh = a.v_sh;
+  bool qk_bf16 = (pl.dtype == kBF16);
+  cudaError_t e;
+  if (pl.need_q16) {
+    __half* y = take((size_t)a.B * a.Sq * a.Hq * a.D * 2);
+    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y,
+                         ds->status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep Q");
+    qs = y;
+    q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
+  }
+  if (pl.need_k16) {
+    __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y,
+                         ds->status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep K");
+    ks = y;
+    k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
+  }
+  if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
+  if (pl.need_v16) {
+    __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+    e = launch_prep_fp16(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, nullptr, nullptr,
+                         y, ds->status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep V");
+    vs = y;
+    v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
+  }
+  CUtensorMap tq, tk, tv;
+  fa_status st = encode_map(&tq, qs, qk_bf16, a.D, a.Hq, a.Sq, a.B, q_sb, q_ss, q_sh);
+  if (st != FA_OK) return st;
+  st = encode_map(&tk, ks, qk_bf16, a.D, a.Hk, a.Sk, a.B, k_sb, k_ss, k_sh);
+  if (st != FA_OK) return st;
+  st = encode_map(&tv, vs, false, a.D, a.Hk, a.Sk, a.B, v_sb, v_ss, v_sh);
+  if (st != FA_OK) return st;
+  a.n_q_tiles = (a.q_end - a.q_begin + 127) / 128;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  if (g_timing) {
+    FA_CUDA(cudaEventCreate(&ev0));
+    FA_CUDA(cudaEventCreate(&ev1));
+    FA_CUDA(cudaEventRecord(ev0, stream));
+  }
+  e = launch_attn_sm100(a, tq, tk, tv, qk_bf16, pl.out_dtype, stream);
+  if (g_timing) {
+    FA_CUDA(cudaEventRecord(ev1, stream));
+    g_events.emplace_back(ev0, ev1);
+  }
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (tensor-core kernel)");
+}
+
+}  // namespace
+
+void note_launch() { ++g_launches; }
+
+}  // namespace fa
+
+using namespace fa;
+
+extern "C" {
+
+void fa_params_init(fa_params* p) {
+  if (!p) return;
+  std::memset(p, 0, sizeof(*p));
+  p->window_left = -1;
+  p->window_right = -1;
+  p->dtype = FA_F16;
+  p->out_dtype = -1;
+}
+
+fa_status fa_init(int device) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fail(FA_ERR_NO_DEVICE, "no CUDA device visible");
+  }
+  if (device < 0 || device >= n) return fail(FA_ERR_INVALID_ARG, "device index out of range");
+  FA_CUDA(cudaSetDevice(device));
+  DeviceState* ds = nullptr;
+  return device_state(&ds);
+}
+
+fa_status fa_device_info(int device, char* name, size_t name_len, uint64_t* total_mem, int* initialized) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    if (name && name_len) std::snprintf(name, name_len, "%s", "No device");
+    if (total_mem) *total_mem = 0;
+    if (initialized) *initialized = 0;
+    return fail(FA_ERR_NO_DEVICE, "no CUDA device visible");
+  }
+  if (device < 0 || device >= n) return fail(FA_ERR_INVALID_ARG, "device index out of range");
+  cudaDeviceProp prop;
+  FA_CUDA(cudaGetDeviceProperties(&prop, device));
+  if (name && name_len) std::snprintf(name, name_len, "%s", prop.name);
+  if (total_mem) *total_mem = (uint64_t)prop.totalGlobalMem;
+  if (initialized) {
+    std::lock_guard<std::mutex> g(g_devices_mu);
+    auto it = g_devices.find(device);
+    *initialized = (it != g_devices.end() && it->second && it->second->ready) ? 1 : 0;
+  }
+  return FA_OK;
+}
+
+size_t fa_workspace_size(const fa_params* p) {
+  Plan pl;
+  if (make_plan(p, &pl) != FA_OK) return 0;
+  return pl.ws_bytes;
+}
+
+size_t fa_tensor_bytes(uint32_t batch, uint32_t seq, uint32_t heads, uint32_t dim, int32_t dtype) {
+  return (size_t)batch * seq * heads * dim * dtype_size(dtype);
+}
+
+fa_status fa_forward(const fa_params* p, const void* q, const void* k, const void* v, void* o,
+                     float* lse, const float* cos, const float* sin, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  Plan pl;
+  fa_status st = make_plan(p, &pl);
+  if (st != FA_OK) return st;
+  DeviceState* ds = nullptr;
+  st = device_state(&ds);
+  if (st != FA_OK) return st;
+  pl.a.o = o;
+  pl.a.lse = lse;
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+}
+
+fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k, const void* v,
+                             float* o_partial, float* lse_partial, const float* cos, const float* sin,
+                             uint32_t q_begin, uint32_t q_end, uint32_t kv_begin, uint32_t kv_end,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+  if (!p) return fail(FA_ERR_INVALID_ARG, "params is NULL");
+  fa_params pp = *p;
+  pp.out_dtype = FA_F32;
+  pp.o_stride[0] = pp.o_stride[1] = pp.o_stride[2] = 0;
+  Plan pl;
+  fa_status st = make_plan(&pp, &pl);
+  if (st != FA_OK) return st;
+  if (q_begin > q_end || q_end > p->seqlen_q || kv_begin > kv_end || kv_end > p->seqlen_k)
+    return fail(FA_ERR_INVALID_ARG, "partial ranges out of bounds");
+  if (!lse_partial) return fail(FA_ERR_INVALID_ARG, "lse_partial is required");
+  DeviceState* ds = nullptr;
+  st = device_state(&ds);
+  if (st != FA_OK) return st;
+  pl.a.q_begin = (int)q_begin;
+  pl.a.q_end = (int)q_end;
+  pl.a.kv_begin = (int)kv_begin;
+  pl.a.kv_end = (int)kv_end;
+  pl.a.o = o_partial;
+  pl.a.lse = lse_partial;
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+}
+
+fa_status fa_combine(const fa_params* p, const float* o_parts, const float* lse_parts, int32_t n_splits,
+                     void* o, float* lse, uint32_t q_begin, uint32_t q_end, void* stream) {
+  Plan pl;
+  fa_status st = make_plan(p, &pl);
+  if (st != FA_OK) return st;
+  if (n_splits <= 0 || !o_parts || !lse_parts || !o) return fail(FA_ERR_INVALID_ARG, "bad combine arguments");
+  if (q_begin > q_end || q_end > p->seqlen_q) return fail(FA_ERR_INVALID_ARG, "row range out of bounds");
+  DeviceState* ds = nullptr;
+  st = device_state(&ds);
+  if (st != FA_OK) return st;
+  pl.a.q_begin = (int)q_begin;
+  pl.a.q_end = (int)q_end;
+  pl.a.o = o;
+  pl.a.lse = lse;
+  cudaError_t e = launch_combine(pl.a, o_parts, lse_parts, n_splits, pl.out_dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "combine");
+}
+
+fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, const void* v, void* o,
+                          float* lse, const float* cos, const float* sin) {
+  Plan pl;
+  fa_status st = make_plan(p, &pl);
+  if (st != FA_OK) return st;
+  if (!q || !k || !v || !o) return fail(FA_ERR_INVALID_ARG, "NULL host pointer");
+  DeviceState* ds = nullptr;
+  st = device_state(&ds);
+  if (st != FA_OK) return st;
+  const AttnArgs& a = pl.a;
+  // Host buffers are taken as contiguous BSHD (the reference assumes C order too).
+  if (p->q_stride[0] || p->k_stride[0] || p->v_stride[0] || p->o_stride[0] || p->q_stride[1] ||
+      p->k_stride[1] || p->v_stride[1] || p->o_stride[1])
+    return fail(FA_ERR_INVALID_ARG, "host-pointer path takes contiguous tensors only");
+  const size_t in_sz = dtype_size(pl.dtype), out_sz = dtype_size(pl.out_dtype);
+  const size_t q_bytes = (size_t)a.B * a.Sq * a.Hq * a.D * in_sz;
+  const size_t k_bytes = (size_t)a.B * a.Sk * a.Hk * a.D * in_sz;
+  const size_t o_bytes = (size_t)a.B * a.Sq * a.Hq * a.D * out_sz;
+  const size_t lse_bytes = (size_t)a.B * a.Hq * a.Sq * sizeof(float);
+  const size_t tab_bytes = (size_t)(a.Sq > a.Sk ? a.Sq : a.Sk) * (a.D / 2) * sizeof(float);
+  const bool tables = p->has_rotary && cos && sin;
+  cudaStream_t s = ds->host_stream;
+  Lease dq(&ds->pool, q_bytes), dk(&ds->pool, k_bytes), dv(&ds->pool, k_bytes), dout(&ds->pool, o_bytes),
+      dl(&ds->pool, lse ? lse_bytes : 0), dc(&ds->pool, tables ? tab_bytes : 0),
+      dsn(&ds->pool, tables ? tab_bytes : 0), dws(&ds->pool, pl.ws_bytes);
+  if ((q_bytes && !dq.p) || (k_bytes && (!dk.p || !dv.p)) || (o_bytes && !dout.p) || (lse && lse_bytes && !dl.p) ||
+      (tables && tab_bytes && (!dc.p || !dsn.p)) || (pl.ws_bytes && !dws.p))
+    return fail(FA_ERR_CUDA, "device allocation failed");
+  if (q_bytes) FA_CUDA(cudaMemcpyAsync(dq.p, q, q_bytes, cudaMemcpyHostToDevice, s));
+  if (k_bytes) {
+    FA_CUDA(cudaMemcpyAsync(dk.p, k, k_bytes, cudaMemcpyHostToDevice, s));
+    FA_CUDA(cudaMemcpyAsync(dv.p, v, k_bytes, cudaMemcpyHostToDevice, s));
+  }
+  if (tables && tab_bytes) {
+    FA_CUDA(cudaMemcpyAsync(dc.p, cos, tab_bytes, cudaMemcpyHostToDevice, s));
+    FA_CUDA(cudaMemcpyAsync(dsn.p, sin, tab_bytes, cudaMemcpyHostToDevice, s));
+  }
+  pl.a.o = dout.p;
+  pl.a.lse = static_cast<float*>(dl.p);
+  st = run(pl, dq.p ? dq.p : (const void*)1, dk.p ? dk.p : (const void*)1, dv.p ? dv.p : (const void*)1,
+           tables ? static_cast<const float*>(dc.p) : nullptr, tables ? static_cast<const float*>(dsn.p) : nullptr,
+           dws.p, pl.ws_bytes, s, ds);
+  if (st != FA_OK) {
+    cudaStreamSynchronize(s);
+    return st;
+  }
+  if (o_bytes) FA_CUDA(cudaMemcpyAsync(o, dout.p, o_bytes, cudaMemcpyDeviceToHost, s));
+  if (lse && lse_bytes) FA_CUDA(cudaMemcpyAsync(lse, dl.p, lse_bytes, cudaMemcpyDeviceToHost, s));
+  FA_CUDA(cudaStreamSynchronize(s));
+  return fa_check_device_status();
+}
+
+fa_status fa_rope_tables(float* cos_out, float* sin_out, uint32_t rows, uint32_t head_dim, float theta) {
+  if (!cos_out || !sin_out || head_dim == 0 || head_dim % 2 || !(theta > 0.f))
+    return fail(FA_ERR_INVALID_ARG, "bad rope table arguments");
+  const uint32_t half = head_dim / 2;
+  for (uint32_t i = 0; i < half; ++i) {
+    const double inv_freq = std::pow((double)theta, -2.0 * (double)i / (double)head_dim);
+    for (uint32_t pos = 0; pos < rows; ++pos) {
+      const double ang = (double)pos * inv_freq;
+      cos_out[(size_t)pos * half + i] = (float)std::cos(ang);
+      sin_out[(size_t)pos * half + i] = (float)std::sin(ang);
+    }
+  }
+  return FA_OK;
+}
+
+fa_status fa_pool_stats(uint64_t* hits, uint64_t* misses, uint64_t* bytes_reserved) {
+  DeviceState* ds = nullptr;
+  fa_status st = device_state(&ds);
+  if (st != FA_OK) return st;
+  ds->pool.stats(hits, misses, bytes_reserved);
+  return FA_OK;
+}
+
+fa_status fa_pool_clear(void) {
+  DeviceState* ds = nullptr;
+  fa_status st = device_state(&ds);
+  if (st != FA_OK) return st;
+  FA_CUDA(cudaDeviceSynchronize());
+  ds->pool.clear();
+  return FA_OK;
+}
+
+fa_status fa_check_device_status(void) {
+  DeviceState* ds = nullptr;
+  fa_status st = device_state(&ds);
+  if (st != FA_OK) return st;
+  unsigned v = 0;
+  FA_CUDA(cudaMemcpy(&v, ds->status, sizeof(v), cudaMemcpyDeviceToHost));
+  if (v == 0) return FA_OK;
+  FA_CUDA(cudaMemset(ds->status, 0, sizeof(unsigned)));
+  if (v & fa::FA_DEV_TIMEOUT)
+    return fail(FA_ERR_TIMEOUT, "a kernel wait exceeded its time limit; the kernel returned early and its output is invalid");
+  return fail(FA_ERR_RANGE, "an input value is outside the fp16 range used internally for bf16 inputs (|x| > 65504)");
+}
+
+uint64_t fa_launch_count(void) { return g_launches; }
+
+fa_status fa_kernel_timing_enable(void) {
+  for (auto& ev : g_events) {
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+  }
+  g_events.clear();
+  g_timing = true;
+  return FA_OK;
+}
+
+fa_status fa_kernel_timing_read(double* total_ms, uint64_t* launches) {
+  double tot = 0.0;
+  fa_status st = FA_OK;
+  for (auto& ev : g_events) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(ev.second);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, ev.first, ev.second);
+    if (e != cudaSuccess && st == FA_OK) st = cuda_fail(e, "kernel timing");
+    tot += ms;
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+  }
+  if (total_ms) *total_ms = tot;
+  if (launches) *launches = g_events.size();
+  g_events.clear();
+  g_timing = false;
+  return st;
+}
+
+const char* fa_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"

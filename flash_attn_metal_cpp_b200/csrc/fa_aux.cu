@@ -1,0 +1,268 @@
+// fa_aux.cu - memory-bound helper kernels around the attention kernels:
+//   * prep_fp16:   rotate-half RoPE (common.metal:150-167) and/or conversion
+//                  to fp16, producing the contiguous fp16 operands the
+//                  tensor-core kernel loads with TMA;
+//   * rope_table:  cos/sin tables [rows, D/2] (layout of the reference's
+//                  host tables, src/flash_attn_core.cpp:343-349), computed
+//                  in double and rounded to float;
+//   * combine:     merge of split-KV partials (O_j, LSE_j);
+//   * fill_empty:  O = 0, LSE = -inf when there is no key at all.
+#include "fa_internal.h"
+#include "fa_ptx.cuh"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+namespace fa {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&x)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&x)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  const __half2* h = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&x)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    x[2 * i] = f.x;
+    x[2 * i + 1] = f.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&x)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0];
+  const float4 b = reinterpret_cast<const float4*>(p)[1];
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+__device__ __forceinline__ bool store8_half(__half* p, const float (&x)[8]) {
+  uint4 w;
+  w.x = pack_half2(x[0], x[1]);
+  w.y = pack_half2(x[2], x[3]);
+  w.z = pack_half2(x[4], x[5]);
+  w.w = pack_half2(x[6], x[7]);
+  *reinterpret_cast<uint4*>(p) = w;
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ok &= fabsf(x[i]) <= 65504.f;
+  return ok;
+}
+
+// One thread = 8 columns of the first half and (with RoPE) the matching 8
+// columns of the second half of one (b, s, h) row. Requires D % 16 == 0.
+template <typename T, bool ROPE>
+__global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss, int64_t sh, int S,
+                                 int H, int D, long long n_rows, const float* __restrict__ cs,
+                                 const float* __restrict__ sn, __half* __restrict__ y,
+                                 unsigned* status) {
+  const int chunks = ROPE ? D / 16 : D / 8;
+  const long long total = n_rows * chunks;
+  bool ok = true;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long rowi = idx / chunks;
+    const int ch = (int)(idx - rowi * chunks);
+    const int h = (int)(rowi % H);
+    const long long bs = rowi / H;
+    const int s = (int)(bs % S);
+    const int b = (int)(bs / S);
+    const T* src = x + (int64_t)b * sb + (int64_t)s * ss + (int64_t)h * sh;
+    __half* dst = y + rowi * D;
+    if (ROPE) {
+      const int half = D / 2;
+      const int c0 = ch * 8;
+      float a[8], bb[8];
+      load8<T>(src + c0, a);
+      load8<T>(src + c0 + half, bb);
+      const float4* cp = reinterpret_cast<const float4*>(cs + (int64_t)s * half + c0);
+      const float4* sp = reinterpret_cast<const float4*>(sn + (int64_t)s * half + c0);
+      const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
+      const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+      const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
+      float ra[8], rb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        ra[i] = a[i] * cv[i] - bb[i] * sv[i];
+        rb[i] = a[i] * sv[i] + bb[i] * cv[i];
+      }
+      ok &= store8_half(dst + c0, ra);
+      ok &= store8_half(dst + c0 + half, rb);
+    } else {
+      float a[8];
+      load8<T>(src + ch * 8, a);
+      ok &= store8_half(dst + ch * 8, a);
+    }
+  }
+  if (!ok) atomicOr(status, FA_DEV_RANGE);
+}
+
+template <typename T>
+cudaError_t prep_t(const void* x, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H, int D,
+                   const float* cs, const float* sn, __half* y, unsigned* status, cudaStream_t st) {
+  const long long n_rows = (long long)B * S * H;
+  const long long total = n_rows * (cs ? D / 16 : D / 8);
+  if (total == 0) return cudaSuccess;
+  const int threads = 256;
+  long long blocks = (total + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (cs)
+    prep_fp16_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(
+        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, status);
+  else
+    prep_fp16_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(
+        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, status);
+  note_launch();
+  return cudaGetLastError();
+}
+
+__global__ void rope_table_kernel(float* cs, float* sn, int rows, int D, double theta) {
+  const int half = D / 2;
+  const long long total = (long long)rows * half;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int i = (int)(idx % half);
+    const long long pos = idx / half;
+    const double inv_freq = pow(theta, -2.0 * (double)i / (double)D);
+    const double ang = (double)pos * inv_freq;
+    double s, c;
+    sincos(ang, &s, &c);
+    cs[idx] = (float)c;
+    sn[idx] = (float)s;
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT cvt_out(float x);
+template <>
+__device__ __forceinline__ float cvt_out<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half cvt_out<__half>(float x) { return __float2half_rn(x); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// One warp per (b, q, h) row of the query range.
+template <typename OutT>
+__global__ void combine_kernel(const AttnArgs a, const float* __restrict__ o_parts,
+                               const float* __restrict__ lse_parts, int n_splits) {
+  const int nq = a.q_end - a.q_begin;
+  const long long rows = (long long)a.B * nq * a.Hq;
+  const long long warp_id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp_id >= rows) return;
+  const int h = (int)(warp_id % a.Hq);
+  const long long bq = warp_id / a.Hq;
+  const int q = a.q_begin + (int)(bq % nq);
+  const int b = (int)(bq / nq);
+  const long long lse_stride = (long long)a.B * a.Hq * a.Sq;
+  const long long o_stride = (long long)a.B * a.Sq * a.Hq * a.D;
+  const long long lse_idx = ((long long)b * a.Hq + h) * a.Sq + q;
+  const long long o_row = (((long long)b * a.Sq + q) * a.Hq + h) * a.D;
+  float mx = -INFINITY;
+  for (int j = 0; j < n_splits; ++j) mx = fmaxf(mx, lse_parts[j * lse_stride + lse_idx]);
+  float w_sum = 0.f;
+  for (int j = 0; j < n_splits; ++j) {
+    const float l = lse_parts[j * lse_stride + lse_idx];
+    w_sum += (l == -INFINITY) ? 0.f : expf(l - mx);
+  }
+  const float lse = (w_sum > 0.f) ? mx + logf(w_sum) : -INFINITY;
+  OutT* orow = reinterpret_cast<OutT*>(a.o) + (int64_t)b * a.o_sb + (int64_t)q * a.o_ss +
+               (int64_t)h * a.o_sh;
+  for (int d = lane; d < a.D; d += 32) {
+    float acc = 0.f;
+    for (int j = 0; j < n_splits; ++j) {
+      const float l = lse_parts[j * lse_stride + lse_idx];
+      if (l != -INFINITY) acc += expf(l - lse) * o_parts[j * o_stride + o_row + d];
+    }
+    orow[d] = cvt_out<OutT>(acc);
+  }
+  if (lane == 0 && a.lse != nullptr) a.lse[lse_idx] = lse;
+}
+
+template <typename OutT>
+__global__ void fill_empty_kernel(const AttnArgs a) {
+  const int nq = a.q_end - a.q_begin;
+  const long long total = (long long)a.B * nq * a.Hq * a.D;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % a.D);
+    const long long r = idx / a.D;
+    const int h = (int)(r % a.Hq);
+    const long long bq = r / a.Hq;
+    const int q = a.q_begin + (int)(bq % nq);
+    const int b = (int)(bq / nq);
+    OutT* orow = reinterpret_cast<OutT*>(a.o) + (int64_t)b * a.o_sb + (int64_t)q * a.o_ss +
+                 (int64_t)h * a.o_sh;
+    orow[d] = cvt_out<OutT>(0.f);
+    if (d == 0 && a.lse != nullptr) a.lse[((long long)b * a.Hq + h) * a.Sq + q] = -INFINITY;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B,
+                             int S, int H, int D, const float* cs, const float* sn, __half* y,
+                             unsigned* status, cudaStream_t st) {
+  switch (in_dtype) {
+    case kF16: return prep_t<__half>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
+    case kBF16: return prep_t<__nv_bfloat16>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
+    default: return prep_t<float>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
+  }
+}
+
+cudaError_t launch_rope_table(float* cs, float* sn, int rows, int D, double theta, cudaStream_t st) {
+  const long long total = (long long)rows * (D / 2);
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  rope_table_kernel<<<(unsigned)blocks, 256, 0, st>>>(cs, sn, rows, D, theta);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const AttnArgs& a, const float* o_parts, const float* lse_parts,
+                           int n_splits, int out_dtype, cudaStream_t st) {
+  const long long rows = (long long)a.B * (a.q_end - a.q_begin) * a.Hq;
+  if (rows <= 0) return cudaSuccess;
+  const int threads = 256;
+  const long long blocks = (rows * 32 + threads - 1) / threads;
+  switch (out_dtype) {
+    case kF16: combine_kernel<__half><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
+    case kBF16: combine_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
+    default: combine_kernel<float><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_empty(const AttnArgs& a, int out_dtype, cudaStream_t st) {
+  const long long total = (long long)a.B * (a.q_end - a.q_begin) * a.Hq * a.D;
+  if (total <= 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  switch (out_dtype) {
+    case kF16: fill_empty_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+    case kBF16: fill_empty_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+    default: fill_empty_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(a); break;
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+}  // namespace fa

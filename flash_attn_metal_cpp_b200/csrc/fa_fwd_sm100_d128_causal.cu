@@ -1,0 +1,14 @@
+// Instantiations of the tcgen05 attention kernel for head_dim 128, causal.
+#include "fa_fwd_sm100.cuh"
+
+namespace fa {
+namespace sm100 {
+
+cudaError_t launch_d128_causal(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+                            const CUtensorMap& tv, bool qk_bf16, int out_dtype, cudaStream_t stream) {
+  return qk_bf16 ? launch_out<128, true, true>(a, tq, tk, tv, out_dtype, stream)
+                 : launch_out<128, true, false>(a, tq, tk, tv, out_dtype, stream);
+}
+
+}  // namespace sm100
+}  // namespace fa

@@ -1,0 +1,69 @@
+// fa_internal.h - declarations shared by the host dispatcher and the kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+namespace fa {
+
+// Problem description handed to every attention kernel. Sizes are
+// validated on the host; strides are in elements.
+struct AttnArgs {
+  int B, Sq, Sk, Hq, Hk, D;
+  int group;               // Hq / Hk
+  float scale;             // softmax_scale as given
+  float scale_log2;        // softmax_scale * log2(e)
+  int causal;              // top-left causal mask: key k masked for query q iff k > q
+  int q_begin, q_end;      // query rows computed (partial API); [0, Sq) otherwise
+  int kv_begin, kv_end;    // keys visited (split-KV); [0, Sk) otherwise
+  int n_q_tiles;           // tiles of the query range for the launch
+  // Direct pointers (SIMT kernel and epilogues).
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t q_sb, q_ss, q_sh;
+  int64_t k_sb, k_ss, k_sh;
+  int64_t v_sb, v_ss, v_sh;
+  void* o;
+  int64_t o_sb, o_ss, o_sh;
+  float* lse;              // [B, Hq, Sq] (NULL = not written)
+  const float* rope_cos;   // [rows, D/2] (SIMT kernel applies RoPE on load when non-NULL)
+  const float* rope_sin;
+  unsigned* status;        // device status word (timeouts, range errors)
+};
+
+// Element type codes shared with fa_b200.h.
+enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
+
+// Tensor-core path: Q/K/V described by TMA maps over 16-bit tensors.
+// qk_bf16: Q and K are bf16 (else fp16); V is always fp16.
+cudaError_t launch_attn_sm100(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
+                              const CUtensorMap& tv, bool qk_bf16, int out_dtype,
+                              cudaStream_t stream);
+
+// Generic CUDA-core path: any head_dim <= 256, fp32/fp16/bf16 inputs.
+cudaError_t launch_attn_simt(const AttnArgs& a, int in_dtype, int out_dtype, cudaStream_t stream);
+
+// RoPE / format pre-pass: y = rope(x) (if cos != NULL) converted to fp16,
+// written contiguous BSHD. x has strides (sb, ss, sh).
+cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh,
+                             int B, int S, int H, int D, const float* cos, const float* sin,
+                             __half* y, unsigned* status, cudaStream_t stream);
+
+// cos/sin tables [rows, D/2] in float32 from theta, computed in double.
+cudaError_t launch_rope_table(float* cos, float* sin, int rows, int D, double theta,
+                              cudaStream_t stream);
+
+// (O, LSE) merge of n split-KV partials.
+cudaError_t launch_combine(const AttnArgs& a, const float* o_parts, const float* lse_parts,
+                           int n_splits, int out_dtype, cudaStream_t stream);
+
+// Zero-fill O rows and set LSE to -inf (used when there is no key at all).
+cudaError_t launch_fill_empty(const AttnArgs& a, int out_dtype, cudaStream_t stream);
+
+// Per-thread launch counter (incremented by every launch_* above).
+void note_launch();
+
+}  // namespace fa

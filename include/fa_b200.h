@@ -1,0 +1,197 @@
+/*
+ * fa_b200.h - C ABI of the B200 (sm_100a) FlashAttention-2 forward library.
+ *
+ * This is the drop-in boundary under the `_flash_attn_metal` Python module.
+ * Every entry point takes plain pointers, sizes and a CUDA stream handle
+ * (passed as void*), so any FFI (ctypes, cffi, pybind11, JNI, cgo) can bind it.
+ *
+ * Reference interfaces replaced (harvestingmoon/flash_attn_metal_cpp):
+ *   fa_params            <- struct FlashAttentionParams     include/flash_attn_core.hpp:31-46
+ *   fa_init              <- MetalDevice::initialize          src/flash_attn_core.cpp:50-64
+ *                           and py_initialize                python/bindings.cpp:42-50
+ *   fa_device_info       <- MetalDevice::device_name / max_buffer_length
+ *                                                            src/flash_attn_core.cpp:83-91
+ *                           and py_get_device_info           python/bindings.cpp:94-109
+ *   fa_forward           <- FlashAttentionForward::execute (kernel part: bind + dispatch)
+ *                                                            src/flash_attn_core.cpp:352-385
+ *   fa_forward_host      <- FlashAttentionForward::execute (whole call: stage in, dispatch,
+ *                           wait, copy out)                  src/flash_attn_core.cpp:276-407
+ *   fa_workspace_size    <- buffer sizing in execute         src/flash_attn_core.cpp:299-305
+ *   fa_tensor_bytes      <- compute_tensor_size              src/flash_attn_core.cpp:445-448
+ *   fa_pool_stats        <- BufferPool hit/miss/bytes stats  include/flash_attn_core.hpp:99-101
+ *   fa_pool_clear        <- BufferPool::clear                src/flash_attn_core.cpp:236-246
+ *   fa_rope_tables       <- host cos/sin tables bound in execute
+ *                                                            src/flash_attn_core.cpp:343-349
+ *   fa_forward_partial   <- (no counterpart) split-KV partial used by the multi-GPU
+ *                           long-context path; same kernel as fa_forward
+ *   fa_combine           <- (no counterpart) (O, LSE) merge of split-KV partials
+ *   fa_last_error        <- std::cerr messages / RuntimeError text
+ *                                                            python/bindings.cpp:46-49,224-232
+ *
+ * Layout contract (same as the reference API, python/bindings.cpp:142-159):
+ *   Q, O : (batch, seqlen_q, num_heads_q, head_dim)   row-major
+ *   K, V : (batch, seqlen_k, num_heads_k, head_dim)   row-major
+ *   LSE  : (batch, num_heads_q, seqlen_q) float32, natural-log log-sum-exp
+ * Element strides may be given per tensor (0 = contiguous BSHD), which
+ * allows zero-copy head/batch slices and (B,H,S,D) tensors.
+ *
+ * Semantics: O = softmax(softmax_scale * Q K^T + mask) V with fp32
+ * accumulation; the causal mask is top-left aligned (key k is masked for
+ * query q iff k > q), as in the reference test oracle (test.py:80-82).
+ * GQA maps query head h to key/value head h / (num_heads_q / num_heads_k).
+ * Rotate-half RoPE is applied to Q and K when has_rotary is set.
+ */
+#ifndef FA_B200_H
+#define FA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fa_status {
+    FA_OK = 0,
+    FA_ERR_INVALID_ARG = 1,   /* bad shape, pointer, stride or alignment */
+    FA_ERR_UNSUPPORTED = 2,   /* valid request that this build does not implement */
+    FA_ERR_CUDA = 3,          /* a CUDA runtime/driver call failed */
+    FA_ERR_TIMEOUT = 4,       /* a bounded in-kernel wait ran out (kernel returned early) */
+    FA_ERR_RANGE = 5,         /* a value left the range of the internal fp16 format */
+    FA_ERR_NOT_INITIALIZED = 6,
+    FA_ERR_NO_DEVICE = 7
+} fa_status;
+
+typedef enum fa_dtype {
+    FA_F16 = 0,
+    FA_BF16 = 1,
+    FA_F32 = 2
+} fa_dtype;
+
+/* Launch parameters. The first block mirrors FlashAttentionParams
+ * (include/flash_attn_core.hpp:31-46) field by field. */
+typedef struct fa_params {
+    uint32_t batch_size;
+    uint32_t seqlen_q;
+    uint32_t seqlen_k;
+    uint32_t num_heads_q;
+    uint32_t num_heads_k;
+    uint32_t head_dim;
+    float softmax_scale;      /* used as given; 0 gives uniform weights, as in the reference */
+    int32_t is_causal;
+    int32_t window_left;      /* -1 = none; any other value is rejected (UNSUPPORTED) */
+    int32_t window_right;     /* -1 = none; any other value is rejected (UNSUPPORTED) */
+    float dropout_p;          /* must be 0 (UNSUPPORTED otherwise) */
+    int32_t has_alibi;        /* must be 0 (UNSUPPORTED otherwise) */
+    int32_t has_rotary;       /* apply rotate-half RoPE to Q and K */
+    uint32_t gqa_group_size;  /* 0 = derive num_heads_q / num_heads_k; else must equal it */
+
+    /* Additions of this library. */
+    int32_t dtype;            /* fa_dtype of Q, K and V */
+    int32_t out_dtype;        /* fa_dtype of O; -1 = same as dtype */
+    float rope_theta;         /* when has_rotary and no cos/sin tables: inv_freq_i = theta^(-2i/D) */
+    /* Element strides (batch, seq, head); the head_dim stride is always 1.
+     * All zero = contiguous BSHD for that tensor. */
+    int64_t q_stride[3];
+    int64_t k_stride[3];
+    int64_t v_stride[3];
+    int64_t o_stride[3];
+} fa_params;
+
+/* Fill `p` with the reference defaults (scale 0, no mask, no RoPE, contiguous). */
+void fa_params_init(fa_params* p);
+
+/* Select and initialise CUDA device `device` for the calling thread. */
+fa_status fa_init(int device);
+
+/* Device name (NUL-terminated, truncated to name_len), total global memory
+ * in bytes, and whether fa_init succeeded on it. Any output may be NULL. */
+fa_status fa_device_info(int device, char* name, size_t name_len,
+                         uint64_t* total_mem, int* initialized);
+
+/* Bytes of device scratch fa_forward needs for `p` (0 when none). */
+size_t fa_workspace_size(const fa_params* p);
+
+/* Bytes of one (B,S,H,D) tensor of element type `dtype`. */
+size_t fa_tensor_bytes(uint32_t batch, uint32_t seq, uint32_t heads,
+                       uint32_t dim, int32_t dtype);
+
+/* Attention forward on device pointers, enqueued on `stream` (cudaStream_t;
+ * NULL = legacy default stream). Returns without synchronising.
+ *   q, k, v   : device inputs (dtype p->dtype)
+ *   o         : device output (dtype p->out_dtype)
+ *   lse       : optional device output [B, Hq, Sq] float32 (NULL = skip)
+ *   cos, sin  : optional device RoPE tables, float32 [max(Sq,Sk), D/2],
+ *               row = position (layout of src/flash_attn_core.cpp:343-349);
+ *               NULL with has_rotary set = build from rope_theta
+ *   workspace : device scratch of fa_workspace_size(p) bytes, or NULL to use
+ *               the library's cached per-device pool. */
+fa_status fa_forward(const fa_params* p, const void* q, const void* k,
+                     const void* v, void* o, float* lse, const float* cos,
+                     const float* sin, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* Whole-call path on HOST pointers: copies Q/K/V (and tables) to device
+ * buffers from the library pool, runs fa_forward, copies O (and LSE when
+ * non-NULL) back and synchronises, like FlashAttentionForward::execute. */
+fa_status fa_forward_host(const fa_params* p, const void* q, const void* k,
+                          const void* v, void* o, float* lse, const float* cos,
+                          const float* sin);
+
+/* Split-KV partial: attention of every query row over the keys in
+ * [kv_begin, kv_end) only (after the causal mask). Writes the row-normalised
+ * partial O (float32, contiguous BSHD) and its LSE [B, Hq, Sq]; rows with no
+ * visible key get O = 0 and LSE = -inf. Only query rows in
+ * [q_begin, q_end) are computed and written. */
+fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k,
+                             const void* v, float* o_partial, float* lse_partial,
+                             const float* cos, const float* sin,
+                             uint32_t q_begin, uint32_t q_end,
+                             uint32_t kv_begin, uint32_t kv_end,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* Merge n_splits partials for rows [q_begin, q_end):
+ *   o_parts   : n_splits consecutive float32 BSHD tensors (Hq heads)
+ *   lse_parts : n_splits consecutive [B, Hq, Sq] float32 arrays
+ *   o         : output of dtype out_dtype (BSHD, p->o_stride honoured)
+ *   lse       : optional merged LSE [B, Hq, Sq] (NULL = skip)
+ * LSE = log sum_j exp(LSE_j), O = sum_j exp(LSE_j - LSE) O_j. */
+fa_status fa_combine(const fa_params* p, const float* o_parts,
+                     const float* lse_parts, int32_t n_splits, void* o,
+                     float* lse, uint32_t q_begin, uint32_t q_end, void* stream);
+
+/* Build float32 cos/sin tables [rows, head_dim/2] on the host:
+ * angle(pos, i) = pos * theta^(-2i/head_dim). */
+fa_status fa_rope_tables(float* cos_out, float* sin_out, uint32_t rows,
+                         uint32_t head_dim, float theta);
+
+/* Device-pool statistics of the calling thread's current device. */
+fa_status fa_pool_stats(uint64_t* hits, uint64_t* misses, uint64_t* bytes_reserved);
+
+/* Free every cached buffer of the calling thread's current device. */
+fa_status fa_pool_clear(void);
+
+/* Read and clear the in-kernel status word of the current device (after the
+ * stream has been synchronised). Returns FA_ERR_TIMEOUT or FA_ERR_RANGE when
+ * a kernel recorded one since the last call, else FA_OK. */
+fa_status fa_check_device_status(void);
+
+/* Number of kernels this library launched on the calling thread so far. */
+uint64_t fa_launch_count(void);
+
+/* Kernel timing (no counterpart in the reference): while enabled, every
+ * launch of the attention kernel on the calling thread is bracketed by CUDA
+ * events recorded on its own stream. fa_kernel_timing_read synchronises
+ * those events and returns the summed duration (ms) and the launch count
+ * since the last enable, then disables timing. */
+fa_status fa_kernel_timing_enable(void);
+fa_status fa_kernel_timing_read(double* total_ms, uint64_t* launches);
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* fa_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_B200_H */
