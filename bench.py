@@ -207,6 +207,7 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg4")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -215,6 +216,8 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     cfg = CONFIGS[args.config]
+    if args.batch is not None:
+        cfg = (args.batch,) + cfg[1:]
 
     if args.impl == "reference":
         return run_reference(args, cfg, rank, world)
