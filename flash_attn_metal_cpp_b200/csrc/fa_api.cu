@@ -727,3 +727,160 @@ fa_status fa_kernel_timing_read(double* total_ms, uint64_t* launches) {
 const char* fa_last_error(void) { return g_last_error.c_str(); }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward (no counterpart in the reference).
+//
+// For callers that must not allocate device memory themselves or through
+// this library: code running inside a host application that owns every
+// device allocation (a plugin whose host forbids cudaMalloc, or a runtime
+// that budgets GPU memory up front). fa_forward_noalloc runs the same
+// kernels as fa_forward, but its scratch (the fp16 staging of Q/K/V and the
+// RoPE tables) lives in the fixed array below instead of a pool buffer.
+//
+// The array is a file-scope __device__ variable of kNoAllocScratchBytes: every
+// GPU on which this module is loaded keeps it until the process exits. In
+// host code its name is only a host-side stand-in, so the device address is
+// taken with cudaGetSymbolAddress once per device (on the first call made
+// with that device current; make that first call before any stream
+// capture). All calls share the array and its contents persist between
+// calls; every byte a call reads is written earlier in the same call, so no
+// clearing is needed. Calls that may overlap on the GPU (different streams,
+// or several host threads) race on the array and must be serialised by the
+// caller.
+namespace fa {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;  // 64 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ unsigned g_noalloc_status;  // kernel status bits of this entry point
+
+struct NoAllocDevice {
+  std::once_flag once;
+  cudaError_t err = cudaSuccess;
+  unsigned char* scratch = nullptr;
+  unsigned* status = nullptr;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_devices[kNoAllocMaxDevices];
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+}  // namespace
+}  // namespace fa
+
+extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const void* k, const void* v,
+                                        void* o, float* lse, const float* cos, const float* sin,
+                                        void* stream_handle) {
+  using namespace fa;
+  Plan pl;
+  fa_status st = make_plan(p, &pl);
+  if (st != FA_OK) return st;
+  AttnArgs& a = pl.a;
+  const bool tables_from_theta = pl.rope && (cos == nullptr || sin == nullptr);
+  const int rows = a.Sq > a.Sk ? a.Sq : a.Sk;
+  const size_t table_bytes = tables_from_theta ? up256((size_t)rows * (a.D / 2) * sizeof(float)) : 0;
+  const size_t need = 2 * table_bytes + pl.ws_bytes;
+  if (need > kNoAllocScratchBytes)
+    return fail(FA_ERR_INVALID_ARG, "fa_forward_noalloc: this problem needs " + std::to_string(need) +
+                                        " bytes of scratch; the allocation-free entry point has a fixed " +
+                                        std::to_string(kNoAllocScratchBytes) + "-byte array (use fa_forward)");
+  if (a.q_end <= a.q_begin || a.B == 0 || a.Hq == 0) return FA_OK;
+  if (!o) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
+
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(FA_ERR_INVALID_ARG, "device index out of range");
+  NoAllocDevice& nd = g_noalloc_devices[dev];
+  std::call_once(nd.once, [&nd]() {
+    nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.scratch), g_noalloc_scratch);
+    if (nd.err == cudaSuccess) nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.status), g_noalloc_status);
+  });
+  if (nd.err != cudaSuccess) return cuda_fail(nd.err, "cudaGetSymbolAddress(scratch)");
+
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
+  a.o = o;
+  a.lse = lse;
+  a.status = nd.status;
+  if (a.kv_end <= a.kv_begin) {
+    e = launch_fill_empty(a, pl.out_dtype, stream);
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "fill_empty");
+  }
+  if (!q || !k || !v) return fail(FA_ERR_INVALID_ARG, "NULL tensor pointer");
+
+  unsigned char* wp = nd.scratch;
+  const float* cs = cos;
+  const float* sn = sin;
+  if (pl.rope && tables_from_theta) {
+    if (!(pl.rope_theta > 0.f) || !std::isfinite(pl.rope_theta))
+      return fail(FA_ERR_INVALID_ARG, "has_rotary needs cos/sin tables or rope_theta > 0");
+    if (a.D % 2 != 0) return fail(FA_ERR_UNSUPPORTED, "RoPE from rope_theta needs an even head_dim");
+    float* tc = reinterpret_cast<float*>(wp);
+    float* ts = reinterpret_cast<float*>(wp + table_bytes);
+    wp += 2 * table_bytes;
+    e = launch_rope_table(tc, ts, rows, a.D, (double)pl.rope_theta, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "rope tables");
+    cs = tc;
+    sn = ts;
+  }
+  if (!pl.rope) cs = sn = nullptr;
+
+  if (!pl.tc) {
+    a.q = q;
+    a.k = k;
+    a.v = v;
+    a.rope_cos = cs;
+    a.rope_sin = sn;
+    e = launch_attn_simt(a, pl.dtype, pl.out_dtype, stream);
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (CUDA-core kernel)");
+  }
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    return fail(FA_ERR_INVALID_ARG, "tensor base addresses must be 16-byte aligned");
+  const void* qs = q;
+  const void* ks = k;
+  const void* vs = v;
+  int64_t q_sb = a.q_sb, q_ss = a.q_ss, q_sh = a.q_sh;
+  int64_t k_sb = a.k_sb, k_ss = a.k_ss, k_sh = a.k_sh;
+  int64_t v_sb = a.v_sb, v_ss = a.v_ss, v_sh = a.v_sh;
+  bool qk_bf16 = (pl.dtype == kBF16);
+  if (pl.need_q16) {
+    __half* y = reinterpret_cast<__half*>(wp);
+    wp += up256((size_t)a.B * a.Sq * a.Hq * a.D * 2);
+    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y, nd.status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep Q");
+    qs = y;
+    q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
+  }
+  if (pl.need_k16) {
+    __half* y = reinterpret_cast<__half*>(wp);
+    wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y, nd.status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep K");
+    ks = y;
+    k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
+  }
+  if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
+  if (pl.need_v16) {
+    __half* y = reinterpret_cast<__half*>(wp);
+    wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+    e = launch_prep_fp16(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, nullptr, nullptr, y,
+                         nd.status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prep V");
+    vs = y;
+    v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
+  }
+  CUtensorMap tq, tk, tv;
+  st = encode_map(&tq, qs, qk_bf16, a.D, a.Hq, a.Sq, a.B, q_sb, q_ss, q_sh);
+  if (st != FA_OK) return st;
+  st = encode_map(&tk, ks, qk_bf16, a.D, a.Hk, a.Sk, a.B, k_sb, k_ss, k_sh);
+  if (st != FA_OK) return st;
+  st = encode_map(&tv, vs, false, a.D, a.Hk, a.Sk, a.B, v_sb, v_ss, v_sh);
+  if (st != FA_OK) return st;
+  a.n_q_tiles = (a.q_end - a.q_begin + 127) / 128;
+  e = launch_attn_sm100(a, tq, tk, tv, qk_bf16, pl.out_dtype, stream);
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (tensor-core kernel)");
+}

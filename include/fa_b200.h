@@ -190,6 +190,26 @@ fa_status fa_kernel_timing_read(double* total_ms, uint64_t* launches);
 /* Text of the last error raised on the calling thread ("" if none). */
 const char* fa_last_error(void);
 
+/* Allocation-free forward. No counterpart in the reference: it exists for
+ * callers that may not allocate device memory, e.g. a plugin inside a host
+ * application that owns every device allocation and forbids cudaMalloc.
+ * Same arguments and results as fa_forward without the workspace: the caller
+ * passes device inputs and outputs, and the library's scratch (fp16 staging
+ * of Q/K/V, RoPE tables built from rope_theta) lives in one fixed 64 MiB
+ * device array that every GPU loading the library's module keeps until the
+ * process exits. Calls no cudaMalloc/cudaFree and no allocating library
+ * routine. A problem whose scratch exceeds 64 MiB is rejected with
+ * FA_ERR_INVALID_ARG and a message giving the size it needs.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make it before any
+ * stream capture. All calls share the array: calls that may overlap on the
+ * GPU (several streams or host threads) race and must be serialised by the
+ * caller. In-kernel timeouts and fp16 range errors of this entry point are
+ * recorded on the device but not reported. */
+fa_status fa_forward_noalloc(const fa_params* p, const void* q, const void* k,
+                             const void* v, void* o, float* lse, const float* cos,
+                             const float* sin, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
