@@ -109,6 +109,8 @@ def attention_ref(
     lse = np.full((B, Hq, Sq), -np.inf, dtype=cd)
     k_lo, k_hi = (0, Sk) if kv_range is None else kv_range
     r_lo, r_hi = (0, Sq) if q_range is None else q_range
+    if k_hi <= k_lo:  # no key at all: softmax over an empty set contributes nothing
+        return (out, lse) if return_lse else out
     keys = np.arange(Sk)
     for b in range(B):
         for h in range(Hq):
