@@ -1,28 +1,35 @@
 // fa_fwd_sm100.cuh - FlashAttention-2 forward kernel for B200 (sm_100a).
 //
-// Computes, per (batch, query head, 128-row query tile), the online-softmax
+// Computes, per (batch, query head, 256-row query block), the online-softmax
 // attention of the reference kernel (kernels/flash_attention_fwd_optimized.metal:79-221:
 // running max m, running sum l, O rescale by exp(m_old - m_new), final O / l),
 // with the score scale applied before the mask (.metal:138-143) and the
 // top-left causal mask (key k masked for query q iff k > q, common.metal:90-92).
 // GQA reads KV head h / group (common.metal:215-217).
 //
-// Blackwell mapping (one CTA = one 128-row query tile, 6 warps):
-//   warp 4      TMA producer: Q tile once, then K_j / V_j tiles into a
-//               NS-stage shared-memory ring (128B-swizzled boxes of 64 cols).
-//   warp 5      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM
-//               S buffers (tcgen05.mma kind::f16, fp32 accumulate), then
-//               O += P_{j-1} V_{j-1} with P read from TMEM (A operand) and V
-//               from shared memory (MN-major B operand).
-//   warps 0-3   softmax: thread t owns query row t = TMEM lane t. Reads S_j
-//               (tcgen05.ld), masks only diagonal / tail tiles, updates the
-//               running max lazily (O is rescaled in TMEM only when the max
-//               grows by more than 2^8), writes P_j = exp2(S*scale*log2e - m)
-//               as fp16 into TMEM (tcgen05.st), and finally normalises O,
-//               writes it with 16-byte stores and writes LSE.
+// Blackwell mapping: one CTA = two 128-row query tiles (t = 0, 1) of one
+// (batch, query head), 12 warps:
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread r of a
+//               warpgroup owns query row r = TMEM lane r of its tile. These two
+//               warpgroups take the registers the third gives up (setmaxnreg).
+//   warp 8      TMA producer: Q_0, Q_1 once, then K_j / V_j into an NS-stage
+//               shared-memory ring (128B-swizzled boxes of 64 columns).
+//   warp 9      MMA issuer (one thread); warps 10-11 idle. Per KV tile j, in this order:
+//               O_0 += P_0 V_{j-1}; S_0 = Q_0 K_j^T; O_1 += P_1 V_{j-1}; S_1 = Q_1 K_j^T
+//               (tcgen05.mma kind::f16, fp32 accumulate in TMEM). While the
+//               tensor cores run one tile's MMAs, the other tile's softmax runs.
+// Softmax of tile t at step j: load the S_t row (tcgen05.ld), mask only
+// diagonal / tail tiles, update the running max lazily (O_t is rescaled in
+// TMEM only when the max grows by more than 2^8), and write
+// P = exp2(S*scale*log2e - m) as fp16 into the first 64 columns of S_t's own
+// TMEM region; the PV MMA reads it from there as its A operand and the next
+// S_t MMA, issued after that PV by the same thread, overwrites it. The S_t
+// commit also covers the previous PV_t, so O_t is stable when the softmax
+// sees S_t. At the end each softmax warpgroup normalises O_t, stores it with
+// 16-byte stores and writes LSE.
 // Causal tiles beyond the diagonal are never loaded or computed.
 //
-// TMEM columns: S0 [0,128) S1 [128,256) O [256,256+D) P [384,448).
+// TMEM columns: S_0/P_0 [0,128) S_1/P_1 [128,256) O_0 [256,256+D) O_1 [384,384+D).
 #pragma once
 #include "fa_internal.h"
 #include "fa_ptx.cuh"
@@ -34,10 +41,17 @@ namespace fa {
 namespace sm100 {
 
 constexpr int BM = 128;          // query rows per tile (= TMEM lanes)
+constexpr int NT = 2;            // query tiles per CTA
 constexpr int BN = 128;          // keys per KV tile
-constexpr int kThreads = 192;    // 4 softmax warps + producer + MMA
+constexpr int kThreads = 384;    // 2 softmax warpgroups + 1 warpgroup with the producer and MMA warps
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+// Register split: launched at 168 per thread (384 x 168 = 64512); the
+// producer/MMA warpgroup drops to 40 and the softmax warpgroups rise to 232:
+// 2 * 128 * 232 + 128 * 40 = 64512, exactly the launch allocation.
+constexpr uint32_t kRegsLaunch = 168, kRegsSoftmax = 232, kRegsOther = 40;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split exceeds launch");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS0 = 0, kColO = 256, kColP = 384;
+constexpr uint32_t kColS = 0, kColO = 256;  // + t * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
 
 template <int D>
@@ -46,19 +60,18 @@ struct Cfg {
   static constexpr int BOX_BYTES = 128 * 128;          // 128 rows x 128 B
   static constexpr int TILE_BYTES = NBOX * BOX_BYTES;  // one Q / K / V tile
   static constexpr int NS = (D == 128) ? 2 : 4;        // K/V pipeline stages
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = TILE_BYTES;
+  static constexpr int OFF_Q = 0;                      // NT query tiles
+  static constexpr int OFF_K = NT * TILE_BYTES;
   static constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
   static constexpr int OFF_BAR = OFF_V + NS * TILE_BYTES;
   static constexpr int SMEM_BYTES = OFF_BAR + 512 + 1024;  // + barriers + alignment slack
 };
 
 struct Bars {
-  uint64_t q_full;
-  uint64_t s_full[2];
-  uint64_t s_free[2];
-  uint64_t p_full;
-  uint64_t o_done;
+  uint64_t q_full[NT];
+  uint64_t s_full[NT];
+  uint64_t p_full[NT];
+  uint64_t o_full[NT];
   uint64_t mma_final;
   uint64_t k_full[4];
   uint64_t v_full[4];
@@ -120,34 +133,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: heaviest causal tiles first, heads of one KV group adjacent.
+  // Work item: heaviest causal blocks first, heads of one KV group adjacent.
+  const int n_blocks = (a.q_end - a.q_begin + NT * BM - 1) / (NT * BM);
   const int hb_count = a.Hq * a.B;
-  const int tile_rank = blockIdx.x / hb_count;
-  const int hb = blockIdx.x - tile_rank * hb_count;
+  const int blk_rank = blockIdx.x / hb_count;
+  const int hb = blockIdx.x - blk_rank * hb_count;
   const int hq = hb % a.Hq;
   const int bz = hb / a.Hq;
-  const int tile = CAUSAL ? (a.n_q_tiles - 1 - tile_rank) : tile_rank;
+  const int blk = CAUSAL ? (n_blocks - 1 - blk_rank) : blk_rank;
   const int hk = hq / a.group;
-  const int q0 = a.q_begin + tile * BM;
-  const int q_last = min(q0 + BM, a.q_end) - 1;
-  int kv_hi = a.kv_end;
-  if (CAUSAL) kv_hi = min(kv_hi, q_last + 1);
-  const int n_kv = (kv_hi > a.kv_begin) ? (kv_hi - a.kv_begin + BN - 1) / BN : 0;
+  const int q0 = a.q_begin + blk * NT * BM;
 
-  const uint32_t b_q_full = smem_addr(&bars->q_full);
-  const uint32_t b_p_full = smem_addr(&bars->p_full);
-  const uint32_t b_o_done = smem_addr(&bars->o_done);
-  const uint32_t b_final = smem_addr(&bars->mma_final);
+  // KV tiles visited by each query tile (0 for a tile with no row in range).
+  int n_kv_t[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) {
+    const int r0 = q0 + t * BM;
+    int n = 0;
+    if (r0 < a.q_end) {
+      int kv_hi = a.kv_end;
+      if (CAUSAL) kv_hi = min(kv_hi, min(r0 + BM, a.q_end));
+      n = (kv_hi > a.kv_begin) ? (kv_hi - a.kv_begin + BN - 1) / BN : 0;
+    }
+    n_kv_t[t] = n;
+  }
+  const int n_kv = max(n_kv_t[0], n_kv_t[1]);
 
-  if (threadIdx.x == 128) {
-    mbar_init(b_q_full, 1);
-    mbar_init(smem_addr(&bars->s_full[0]), 1);
-    mbar_init(smem_addr(&bars->s_full[1]), 1);
-    mbar_init(smem_addr(&bars->s_free[0]), 128);
-    mbar_init(smem_addr(&bars->s_free[1]), 128);
-    mbar_init(b_p_full, 128);
-    mbar_init(b_o_done, 1);
-    mbar_init(b_final, 1);
+  if (threadIdx.x == kProducerWarp * 32) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      mbar_init(smem_addr(&bars->q_full[t]), 1);
+      mbar_init(smem_addr(&bars->s_full[t]), 1);
+      mbar_init(smem_addr(&bars->p_full[t]), 128);
+      mbar_init(smem_addr(&bars->o_full[t]), 1);
+    }
+    mbar_init(smem_addr(&bars->mma_final), 1);
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(smem_addr(&bars->k_full[s]), 1);
       mbar_init(smem_addr(&bars->v_full[s]), 1);
@@ -156,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bars->abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_addr(&bars->tmem_base), kTmemCols);
     tmem_relinquish();
   }
@@ -165,17 +185,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
-
-  if (warp == 4) {
+  if (warp >= 8) {
+  reg_alloc_dec<kRegsOther>();
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && n_kv > 0) {
       prefetch_tmap(&tm_q);
       prefetch_tmap(&tm_k);
       prefetch_tmap(&tm_v);
-      mbar_arrive_expect_tx(b_q_full, C::TILE_BYTES);
 #pragma unroll
-      for (int bx = 0; bx < C::NBOX; ++bx)
-        tma_load_4d(sQ + bx * C::BOX_BYTES, &tm_q, b_q_full, bx * 64, hq, q0, bz);
+      for (int t = 0; t < NT; ++t) {
+        if (n_kv_t[t] == 0) continue;
+        const uint32_t bq = smem_addr(&bars->q_full[t]);
+        mbar_arrive_expect_tx(bq, C::TILE_BYTES);
+#pragma unroll
+        for (int bx = 0; bx < C::NBOX; ++bx)
+          tma_load_4d(sQ + t * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_q, bq, bx * 64, hq, q0 + t * BM, bz);
+      }
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         if (*abort_flag) break;
@@ -199,7 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = j + 1;
       }
       // Never leave the CTA with bulk copies still writing shared memory.
-      fa_wait(b_q_full, 0, a.status);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        if (n_kv_t[t] > 0) fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
       for (int j = max(0, issued - C::NS); j < issued; ++j) {
         const int st = j % C::NS;
         const uint32_t par = (j / C::NS) & 1;
@@ -207,93 +235,90 @@ __global__ void __launch_bounds__(kThreads, 1)
         fa_wait(smem_addr(&bars->v_full[st]), par, a.status);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_kv > 0) {
       constexpr uint32_t fmt_qk = QK_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = make_idesc(BM, BN, fmt_qk, 0, 0);
       constexpr uint32_t idesc_o = make_idesc(BM, D, 0 /*f16*/, 0, 1 /*V is MN-major*/);
-      const uint32_t tS = tmem + kColS0;
-      const uint32_t tO = tmem + kColO;
-      const uint32_t tP = tmem + kColP;
-      bool ok = fa_wait(b_q_full, 0, a.status);
-      tc_fence_after();
-
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i % C::NS;
-        if (!fa_wait(b_p_full, i & 1, a.status)) return false;
-        if (!fa_wait(smem_addr(&bars->v_full[st]), (i / C::NS) & 1, a.status)) return false;
-        tc_fence_after();
-        const uint32_t vbase = sV + st * C::TILE_BYTES;
+      bool ok = true;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          // 16 keys x D cols; D-halves are C::BOX_BYTES apart (LBO), 8-key groups 1024 B (SBO).
-          const uint64_t bdesc = smem_desc(vbase + kk * 16 * 128, C::BOX_BYTES, 1024);
-          mma_ts(tO, tP + kk * 8, bdesc, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(smem_addr(&bars->kv_empty[st]));
-        mma_commit(b_o_done);
-        return true;
-      };
-
-      for (int j = 0; ok && j < n_kv; ++j) {
+      for (int t = 0; t < NT; ++t)
+        if (ok && n_kv_t[t] > 0) ok = fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
+      // j runs one past the last KV tile to issue the final PV of each tile.
+      for (int j = 0; ok && j <= n_kv; ++j) {
         if (*abort_flag) { ok = false; break; }
-        const int st = j % C::NS;
-        const int sb = j & 1;
-        if (!fa_wait(smem_addr(&bars->k_full[st]), (j / C::NS) & 1, a.status)) { ok = false; break; }
-        if (j >= 2 && !fa_wait(smem_addr(&bars->s_free[sb]), ((j - 2) >> 1) & 1, a.status)) {
+        if (j < n_kv && !fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status)) { ok = false; break; }
+        if (j >= 1 && !fa_wait(smem_addr(&bars->v_full[(j - 1) % C::NS]), ((j - 1) / C::NS) & 1, a.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t kbase = sK + st * C::TILE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::BOX_BYTES + (kk & 3) * 32;
-          const uint64_t adesc = smem_desc(sQ + off, 16, 1024);
-          const uint64_t bdesc = smem_desc(kbase + off, 16, 1024);
-          mma_ss(tS + sb * BN, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+        for (int t = 0; t < NT; ++t) {
+          const uint32_t tS = tmem + kColS + t * 128;
+          const uint32_t tO = tmem + kColO + t * 128;
+          if (j >= 1 && j - 1 < n_kv_t[t]) {
+            // O_t += P_t V_{j-1}: P from TMEM (first 64 columns of S_t), V MN-major from smem.
+            const int i = j - 1;
+            if (!fa_wait(smem_addr(&bars->p_full[t]), i & 1, a.status)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t vbase = sV + (i % C::NS) * C::TILE_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const uint64_t bdesc = smem_desc(vbase + kk * 16 * 128, C::BOX_BYTES, 1024);
+              mma_ts(tO, tS + kk * 8, bdesc, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (i == n_kv_t[t] - 1) mma_commit(smem_addr(&bars->o_full[t]));
+          }
+          if (j < n_kv_t[t]) {
+            // S_t = Q_t K_j^T.
+            const uint32_t qbase = sQ + t * C::TILE_BYTES;
+            const uint32_t kbase = sK + (j % C::NS) * C::TILE_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * C::BOX_BYTES + (kk & 3) * 32;
+              mma_ss(tS, smem_desc(qbase + off, 16, 1024), smem_desc(kbase + off, 16, 1024), idesc_s,
+                     kk > 0 ? 1u : 0u);
+            }
+            mma_commit(smem_addr(&bars->s_full[t]));
+          }
         }
-        mma_commit(smem_addr(&bars->s_full[sb]));
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+        if (ok && j >= 1) mma_commit(smem_addr(&bars->kv_empty[(j - 1) % C::NS]));
       }
-      if (ok && !issue_pv(n_kv - 1)) ok = false;
       if (!ok) *abort_flag = 1;
       // All MMAs of this CTA must be complete before TMEM is released.
-      mma_commit(b_final);
-      fa_wait(b_final, 0, a.status);
+      mma_commit(smem_addr(&bars->mma_final));
+      fa_wait(smem_addr(&bars->mma_final), 0, a.status);
     }
+  }
   } else {
-    // ------------------------------------------------------------ softmax warps
-    const int row = threadIdx.x;  // 0..127 == TMEM lane
-    const int row_g = q0 + row;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    // ------------------------------------------------------------ softmax warpgroups
+    reg_alloc_inc<kRegsSoftmax>();
+    const int t = warp >> 2;               // query tile of this warpgroup
+    const int row = threadIdx.x & 127;     // TMEM lane
+    const int row_g = q0 + t * BM + row;
+    const int my_kv = n_kv_t[t];
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const uint32_t tS = lane_base + kColS + t * 128;
+    const uint32_t tO = lane_base + kColO + t * 128;
+    const uint32_t b_s_full = smem_addr(&bars->s_full[t]);
+    const uint32_t b_p_full = smem_addr(&bars->p_full[t]);
     const float sl2 = a.scale_log2;
     float m_run = -INFINITY;  // running max in log2 units (value actually subtracted)
     float l_run = 0.f;
     bool ok = true;
 
-    for (int j = 0; j < n_kv; ++j) {
+    for (int j = 0; j < my_kv; ++j) {
       if (*abort_flag) { ok = false; break; }
-      const int sb = j & 1;
-      bool got = fa_wait(smem_addr(&bars->s_full[sb]), (j >> 1) & 1, a.status);
+      const bool got = fa_wait(b_s_full, j & 1, a.status);
       if (!__all_sync(0xffffffffu, got)) { ok = false; *abort_flag = 1; break; }
       tc_fence_after();
       float s[BN];
-      {
-        uint32_t r[32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(lane_base + kColS0 + sb * BN + c * 32, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(smem_addr(&bars->s_free[sb]));
+      tmem_ld128(tS, s);
 
       const int kv0 = a.kv_begin + j * BN;
-      const bool need_mask = (kv0 + BN > a.kv_end) || (CAUSAL && kv0 + BN - 1 > q0);
+      const bool need_mask = (kv0 + BN > a.kv_end) || (CAUSAL && kv0 + BN - 1 > q0 + t * BM);
       int key_lim = a.kv_end - kv0;                       // keys [kv0, kv0+key_lim) visible
       if (CAUSAL) key_lim = min(key_lim, row_g - kv0 + 1);
       float ext;
@@ -311,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < BN; ++c) ext = fminf(ext, (!need_mask || c < key_lim) ? s[c] : INFINITY);
       }
-      float m_cand = (sl2 == 0.f) ? 0.f : ext * sl2;
+      const float m_cand = (sl2 == 0.f) ? 0.f : ext * sl2;
       const float m_new = fmaxf(m_run, m_cand);
       const bool grow = (m_new > m_run + kRescaleThreshold);
       const bool any_grow = __any_sync(0xffffffffu, grow);
@@ -319,58 +344,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_sub = (m_use == -INFINITY) ? 0.f : m_use;
       const float alpha = (m_use == m_run || m_use == -INFINITY) ? 1.f : ex2_approx(m_run - m_use);
 
-      // PV_{j-1} must be complete before O is rescaled and P is overwritten.
-      if (j > 0) {
-        got = fa_wait(b_o_done, (j - 1) & 1, a.status);
-        if (!__all_sync(0xffffffffu, got)) { ok = false; *abort_flag = 1; break; }
-        tc_fence_after();
-        if (any_grow) {
+      // O_t is stable here: the S_t commit also covered the previous PV_t.
+      if (any_grow && j > 0) {
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(lane_base + kColO + c * 32, r);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tO + c * 32, r);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(lane_base + kColO + c * 32, r);
-          }
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(tO + c * 32, r);
         }
       }
       float rsum = 0.f;
-      uint32_t p[BN / 2];
-      if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-          float p0 = (c < key_lim) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
-          float p1 = (c + 1 < key_lim) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
-          rsum += p0 + p1;
-          p[c / 2] = pack_half2(p0, p1);
-        }
-      } else {
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t p[16];
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < BN; c += 2) {
-          float p0 = ex2_approx(fmaf(s[c], sl2, -m_sub));
-          float p1 = ex2_approx(fmaf(s[c + 1], sl2, -m_sub));
-          rsum += p0 + p1;
-          p[c / 2] = pack_half2(p0, p1);
+          for (int c = c0; c < c0 + 32; c += 2) {
+            const float p0 = (c < key_lim) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
+            const float p1 = (c + 1 < key_lim) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
+            rsum += p0 + p1;
+            p[(c - c0) / 2] = pack_half2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int c = c0; c < c0 + 32; c += 2) {
+            const float p0 = ex2_approx(fmaf(s[c], sl2, -m_sub));
+            const float p1 = ex2_approx(fmaf(s[c + 1], sl2, -m_sub));
+            rsum += p0 + p1;
+            p[(c - c0) / 2] = pack_half2(p0, p1);
+          }
         }
+        tmem_st16(tS + c0 / 2, p);  // P columns [c0/2, c0/2+16) of S_t's region
       }
       l_run = l_run * alpha + rsum;
       m_run = m_use;
-#pragma unroll
-      for (int c = 0; c < BN / 2; c += 16) tmem_st16(lane_base + kColP + c, &p[c]);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(b_p_full);
     }
 
     // ---------------------------------------------------------- epilogue
-    const bool row_ok = (row_g < a.q_end);
-    if (ok && n_kv > 0) {
-      bool got = fa_wait(b_o_done, (n_kv - 1) & 1, a.status);
+    const bool row_ok = (row_g < a.q_end) && (q0 + t * BM < a.q_end);
+    if (ok && my_kv > 0) {
+      const bool got = fa_wait(smem_addr(&bars->o_full[t]), 0, a.status);
       if (!__all_sync(0xffffffffu, got)) { ok = false; *abort_flag = 1; }
       tc_fence_after();
     }
-    if (ok) {
+    if (ok && q0 + t * BM < a.q_end) {
       const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
       if (row_ok && a.lse != nullptr) {
         const float lse = (l_run > 0.f) ? (m_run + log2f(l_run)) * 0.69314718055994531f : -INFINITY;
@@ -381,9 +403,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float v[32];
-        if (n_kv > 0) {
+        if (my_kv > 0) {
           uint32_t r[32];
-          tmem_ld32(lane_base + kColO + c * 32, r);
+          tmem_ld32(tO + c * 32, r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * inv_l;
         } else {
@@ -398,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();  // role branches ran on one lane; reconverge before the CTA barrier
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -411,7 +433,7 @@ cudaError_t launch_t(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap
   constexpr int smem = Cfg<D>::SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  const long long blocks = (long long)a.n_q_tiles * a.Hq * a.B;
+  const long long blocks = (long long)((a.q_end - a.q_begin + NT * BM - 1) / (NT * BM)) * a.Hq * a.B;
   if (blocks <= 0) return cudaSuccess;
   kern<<<dim3((unsigned)blocks), dim3(kThreads), smem, stream>>>(tq, tk, tv, a);
   note_launch();

@@ -172,6 +172,32 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 128 consecutive columns per thread: four x32 loads issued back to back and
+// one tcgen05.wait::ld, all inside one asm statement (outputs valid after it).
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&f)[128]) {
+#define FA_R8(b) "=f"(f[b]), "=f"(f[b + 1]), "=f"(f[b + 2]), "=f"(f[b + 3]), "=f"(f[b + 4]), "=f"(f[b + 5]), \
+                 "=f"(f[b + 6]), "=f"(f[b + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%129];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,"
+      "%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%130];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,"
+      "%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%131];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : FA_R8(0), FA_R8(8), FA_R8(16), FA_R8(24), FA_R8(32), FA_R8(40), FA_R8(48), FA_R8(56), FA_R8(64),
+        FA_R8(72), FA_R8(80), FA_R8(88), FA_R8(96), FA_R8(104), FA_R8(112), FA_R8(120)
+      : "r"(taddr), "r"(taddr + 32), "r"(taddr + 64), "r"(taddr + 96)
+      : "memory");
+#undef FA_R8
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -222,6 +248,16 @@ __host__ __device__ constexpr uint32_t make_idesc(uint32_t m, uint32_t n, uint32
                                                   uint32_t a_mn_major, uint32_t b_mn_major) {
   return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | (a_mn_major << 15) | (b_mn_major << 16) |
          ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// Warpgroup register reallocation (all 128 threads of the warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // ---------------------------------------------------------------- math
