@@ -12,9 +12,10 @@
 //   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread r of a
 //               warpgroup owns query row r = TMEM lane r of its tile. These two
 //               warpgroups take the registers the third gives up (setmaxnreg).
-//   warp 8      TMA producer: Q_0, Q_1 once, then K_j / V_j into an NS-stage
-//               shared-memory ring (128B-swizzled boxes of 64 columns).
-//   warp 9      MMA issuer (one thread); warps 10-11 idle. Per KV tile j, in this order:
+//   warps 8,10  TMA producers: warp 8 loads Q_0, Q_1 once and K_j into an
+//               NS-stage ring, warp 10 loads V_j into its own NS-stage ring
+//               (128B-swizzled boxes of 64 columns).
+//   warp 9      MMA issuer (one thread); warp 11 idle. Per KV tile j, in this order:
 //               O_0 += P_0 V_{j-1}; S_0 = Q_0 K_j^T; O_1 += P_1 V_{j-1}; S_1 = Q_1 K_j^T
 //               (tcgen05.mma kind::f16, fp32 accumulate in TMEM). While the
 //               tensor cores run one tile's MMAs, the other tile's softmax runs.
@@ -44,22 +45,23 @@ constexpr int BM = 128;          // query rows per tile (= TMEM lanes)
 constexpr int NT = 2;            // query tiles per CTA
 constexpr int BN = 128;          // keys per KV tile
 constexpr int kThreads = 384;    // 2 softmax warpgroups + 1 warpgroup with the producer and MMA warps
-constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kProducerWarp = 8, kMmaWarp = 9, kProducerVWarp = 10;
 // Register split: launched at 168 per thread (384 x 168 = 64512); the
-// producer/MMA warpgroup drops to 40 and the softmax warpgroups rise to 232:
-// 2 * 128 * 232 + 128 * 40 = 64512, exactly the launch allocation.
-constexpr uint32_t kRegsLaunch = 168, kRegsSoftmax = 232, kRegsOther = 40;
+// producer/MMA warpgroup drops to 72 and the softmax warpgroups rise to 216:
+// 2 * 128 * 216 + 128 * 72 = 64512, exactly the launch allocation.
+constexpr uint32_t kRegsLaunch = 168, kRegsSoftmax = 216, kRegsOther = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunch, "register split exceeds launch");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;  // + t * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
+constexpr int kPolyPairs = 4;  // of every 16 exp2 pairs, this many run as a polynomial on the FMA pipe
 
 template <int D>
 struct Cfg {
   static constexpr int NBOX = D / 64;                  // 64-col (128 B) boxes per row
   static constexpr int BOX_BYTES = 128 * 128;          // 128 rows x 128 B
   static constexpr int TILE_BYTES = NBOX * BOX_BYTES;  // one Q / K / V tile
-  static constexpr int NS = (D == 128) ? 2 : 4;        // K/V pipeline stages
+  static constexpr int NS = (D == 128) ? 2 : 4;        // stages of the K ring and of the V ring
   static constexpr int OFF_Q = 0;                      // NT query tiles
   static constexpr int OFF_K = NT * TILE_BYTES;
   static constexpr int OFF_V = OFF_K + NS * TILE_BYTES;
@@ -75,7 +77,8 @@ struct Bars {
   uint64_t mma_final;
   uint64_t k_full[4];
   uint64_t v_full[4];
-  uint64_t kv_empty[4];
+  uint64_t k_empty[4];
+  uint64_t v_empty[4];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -171,7 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(smem_addr(&bars->k_full[s]), 1);
       mbar_init(smem_addr(&bars->v_full[s]), 1);
-      mbar_init(smem_addr(&bars->kv_empty[s]), 1);
+      mbar_init(smem_addr(&bars->k_empty[s]), 1);
+      mbar_init(smem_addr(&bars->v_empty[s]), 1);
     }
     bars->abort_flag = 0;
     fence_barrier_init();
@@ -186,61 +190,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars->tmem_base;
   volatile int* abort_flag = &bars->abort_flag;
   if (warp >= 8) {
-  reg_alloc_dec<kRegsOther>();
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0 && n_kv > 0) {
-      prefetch_tmap(&tm_q);
-      prefetch_tmap(&tm_k);
-      prefetch_tmap(&tm_v);
+    reg_alloc_dec<kRegsOther>();
+    if ((warp == kProducerWarp || warp == kProducerVWarp) && lane == 0 && n_kv > 0) {
+      // -------------------------------------------------------- producers
+      // warp 8 streams Q_0, Q_1 and the K ring, warp 10 the V ring. K_j is
+      // released right after the S MMAs of step j, V_j after the PV MMAs of
+      // step j+1, so each ring refills as early as its consumer allows.
+      const bool is_k = (warp == kProducerWarp);
+      const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+      const uint32_t ring = is_k ? sK : sV;
+      uint64_t* full = is_k ? bars->k_full : bars->v_full;
+      uint64_t* empty = is_k ? bars->k_empty : bars->v_empty;
+      prefetch_tmap(tm);
+      if (is_k) {
+        prefetch_tmap(&tm_q);
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (n_kv_t[t] == 0) continue;
-        const uint32_t bq = smem_addr(&bars->q_full[t]);
-        mbar_arrive_expect_tx(bq, C::TILE_BYTES);
+        for (int t = 0; t < NT; ++t) {
+          if (n_kv_t[t] == 0) continue;
+          const uint32_t bq = smem_addr(&bars->q_full[t]);
+          mbar_arrive_expect_tx(bq, C::TILE_BYTES);
 #pragma unroll
-        for (int bx = 0; bx < C::NBOX; ++bx)
-          tma_load_4d(sQ + t * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_q, bq, bx * 64, hq, q0 + t * BM, bz);
+          for (int bx = 0; bx < C::NBOX; ++bx)
+            tma_load_4d(sQ + t * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_q, bq, bx * 64, hq, q0 + t * BM, bz);
+        }
       }
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         if (*abort_flag) break;
         const int st = j % C::NS;
-        const uint32_t use = j / C::NS;
-        if (!fa_wait(smem_addr(&bars->kv_empty[st]), (use + 1) & 1, a.status)) {
+        if (!fa_wait(smem_addr(&empty[st]), ((j / C::NS) + 1) & 1, a.status)) {
           *abort_flag = 1;
           break;
         }
-        const int kv0 = a.kv_begin + j * BN;
-        const uint32_t bk = smem_addr(&bars->k_full[st]);
-        const uint32_t bv = smem_addr(&bars->v_full[st]);
-        mbar_arrive_expect_tx(bk, C::TILE_BYTES);
+        const uint32_t bfull = smem_addr(&full[st]);
+        mbar_arrive_expect_tx(bfull, C::TILE_BYTES);
 #pragma unroll
         for (int bx = 0; bx < C::NBOX; ++bx)
-          tma_load_4d(sK + st * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_k, bk, bx * 64, hk, kv0, bz);
-        mbar_arrive_expect_tx(bv, C::TILE_BYTES);
-#pragma unroll
-        for (int bx = 0; bx < C::NBOX; ++bx)
-          tma_load_4d(sV + st * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_v, bv, bx * 64, hk, kv0, bz);
+          tma_load_4d(ring + st * C::TILE_BYTES + bx * C::BOX_BYTES, tm, bfull, bx * 64, hk,
+                      a.kv_begin + j * BN, bz);
         issued = j + 1;
       }
       // Never leave the CTA with bulk copies still writing shared memory.
+      if (is_k) {
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
-        if (n_kv_t[t] > 0) fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
-      for (int j = max(0, issued - C::NS); j < issued; ++j) {
-        const int st = j % C::NS;
-        const uint32_t par = (j / C::NS) & 1;
-        fa_wait(smem_addr(&bars->k_full[st]), par, a.status);
-        fa_wait(smem_addr(&bars->v_full[st]), par, a.status);
+        for (int t = 0; t < NT; ++t)
+          if (n_kv_t[t] > 0) fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
       }
-    }
-  } else if (warp == kMmaWarp) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && n_kv > 0) {
+      for (int j = max(0, issued - C::NS); j < issued; ++j)
+        fa_wait(smem_addr(&full[j % C::NS]), (j / C::NS) & 1, a.status);
+    } else if (warp == kMmaWarp && lane == 0 && n_kv > 0) {
+      // -------------------------------------------------------- MMA issuer
       constexpr uint32_t fmt_qk = QK_BF16 ? 1u : 0u;
       constexpr uint32_t idesc_s = make_idesc(BM, BN, fmt_qk, 0, 0);
       constexpr uint32_t idesc_o = make_idesc(BM, D, 0 /*f16*/, 0, 1 /*V is MN-major*/);
+      // Descriptor words: the high words are fixed per operand kind; the low
+      // words hold the start address (>> 4), advanced by constant offsets.
+      const uint64_t qk_desc0 = smem_desc(smem_addr(smem), 16, 1024);        // K-major Q / K tiles
+      const uint64_t v_desc0 = smem_desc(sV, C::BOX_BYTES, 1024);             // MN-major V tiles
+      const uint32_t qk_lo0 = (uint32_t)qk_desc0, qk_hi = (uint32_t)(qk_desc0 >> 32);
+      const uint32_t v_lo0 = (uint32_t)v_desc0, v_hi = (uint32_t)(v_desc0 >> 32);
       bool ok = true;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
@@ -248,12 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // j runs one past the last KV tile to issue the final PV of each tile.
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (*abort_flag) { ok = false; break; }
-        if (j < n_kv && !fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status)) { ok = false; break; }
-        if (j >= 1 && !fa_wait(smem_addr(&bars->v_full[(j - 1) % C::NS]), ((j - 1) / C::NS) & 1, a.status)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+        bool k_ready = false, v_ready = false;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           const uint32_t tS = tmem + kColS + t * 128;
@@ -261,37 +264,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= 1 && j - 1 < n_kv_t[t]) {
             // O_t += P_t V_{j-1}: P from TMEM (first 64 columns of S_t), V MN-major from smem.
             const int i = j - 1;
+            if (!v_ready) {
+              if (!fa_wait(smem_addr(&bars->v_full[i % C::NS]), (i / C::NS) & 1, a.status)) { ok = false; break; }
+              v_ready = true;
+            }
             if (!fa_wait(smem_addr(&bars->p_full[t]), i & 1, a.status)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t vbase = sV + (i % C::NS) * C::TILE_BYTES;
+            // 16 keys x D cols per MMA: D-halves C::BOX_BYTES apart (LBO), 8-key groups 1024 B (SBO).
+            const uint32_t v_lo = v_lo0 + (uint32_t)((i % C::NS) * C::TILE_BYTES >> 4);
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              const uint64_t bdesc = smem_desc(vbase + kk * 16 * 128, C::BOX_BYTES, 1024);
-              mma_ts(tO, tS + kk * 8, bdesc, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < BN / 16; ++kk)
+              mma_ts_lohi(tO, tS + kk * 8, v_lo + kk * (16 * 128 >> 4), v_hi, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
             if (i == n_kv_t[t] - 1) mma_commit(smem_addr(&bars->o_full[t]));
           }
           if (j < n_kv_t[t]) {
             // S_t = Q_t K_j^T.
-            const uint32_t qbase = sQ + t * C::TILE_BYTES;
-            const uint32_t kbase = sK + (j % C::NS) * C::TILE_BYTES;
+            if (!k_ready) {
+              if (!fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status)) { ok = false; break; }
+              k_ready = true;
+            }
+            tc_fence_after();
+            const uint32_t q_lo = qk_lo0 + (uint32_t)((C::OFF_Q + t * C::TILE_BYTES) >> 4);
+            const uint32_t k_lo = qk_lo0 + (uint32_t)((C::OFF_K + (j % C::NS) * C::TILE_BYTES) >> 4);
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * C::BOX_BYTES + (kk & 3) * 32;
-              mma_ss(tS, smem_desc(qbase + off, 16, 1024), smem_desc(kbase + off, 16, 1024), idesc_s,
-                     kk > 0 ? 1u : 0u);
+              const uint32_t off = ((kk >> 2) * C::BOX_BYTES + (kk & 3) * 32) >> 4;
+              mma_ss_lohi(tS, q_lo + off, qk_hi, k_lo + off, qk_hi, idesc_s, kk > 0 ? 1u : 0u);
             }
             mma_commit(smem_addr(&bars->s_full[t]));
           }
         }
-        if (ok && j >= 1) mma_commit(smem_addr(&bars->kv_empty[(j - 1) % C::NS]));
+        if (!ok) break;
+        if (k_ready) mma_commit(smem_addr(&bars->k_empty[j % C::NS]));
+        if (v_ready) mma_commit(smem_addr(&bars->v_empty[(j - 1) % C::NS]));
       }
       if (!ok) *abort_flag = 1;
       // All MMAs of this CTA must be complete before TMEM is released.
       mma_commit(smem_addr(&bars->mma_final));
       fa_wait(smem_addr(&bars->mma_final), 0, a.status);
     }
-  }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
     reg_alloc_inc<kRegsSoftmax>();
@@ -322,15 +333,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int key_lim = a.kv_end - kv0;                       // keys [kv0, kv0+key_lim) visible
       if (CAUSAL) key_lim = min(key_lim, row_g - kv0 + 1);
       float ext;
-      if (sl2 >= 0.f) {
+      if (!need_mask && sl2 > 0.f) {
+        ext = row_max128(s);  // hot path: full tile, positive scale
+      } else if (sl2 >= 0.f) {
         ext = -INFINITY;
-        if (need_mask) {
 #pragma unroll
-          for (int c = 0; c < BN; ++c) ext = fmaxf(ext, c < key_lim ? s[c] : -INFINITY);
-        } else {
-#pragma unroll
-          for (int c = 0; c < BN; ++c) ext = fmaxf(ext, s[c]);
-        }
+        for (int c = 0; c < BN; ++c) ext = fmaxf(ext, (!need_mask || c < key_lim) ? s[c] : -INFINITY);
       } else {
         ext = INFINITY;
 #pragma unroll
@@ -355,29 +363,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(tO + c * 32, r);
         }
       }
-      float rsum = 0.f;
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+      const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_sub, -m_sub);
 #pragma unroll
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t p[16];
         if (need_mask) {
 #pragma unroll
-          for (int c = c0; c < c0 + 32; c += 2) {
+          for (int i = 0; i < 16; ++i) {
+            const int c = c0 + 2 * i;
             const float p0 = (c < key_lim) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
             const float p1 = (c + 1 < key_lim) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
-            rsum += p0 + p1;
-            p[(c - c0) / 2] = pack_half2(p0, p1);
+            acc0 = __fadd2_rn(acc0, make_float2(p0, p1));
+            p[i] = pack_half2(p0, p1);
           }
         } else {
 #pragma unroll
-          for (int c = c0; c < c0 + 32; c += 2) {
-            const float p0 = ex2_approx(fmaf(s[c], sl2, -m_sub));
-            const float p1 = ex2_approx(fmaf(s[c + 1], sl2, -m_sub));
-            rsum += p0 + p1;
-            p[(c - c0) / 2] = pack_half2(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const int c = c0 + 2 * i;
+            const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sc2, nm2);
+            // kPolyPairs of every 16 pairs go to the FMA pipe, the rest to MUFU.
+            const float2 e = (i < kPolyPairs) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if (i & 1) acc1 = __fadd2_rn(acc1, e);
+            else acc0 = __fadd2_rn(acc0, e);
+            p[i] = pack_half2(e.x, e.y);
           }
         }
         tmem_st16(tS + c0 / 2, p);  // P columns [c0/2, c0/2+16) of S_t's region
       }
+      const float rsum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
       l_run = l_run * alpha + rsum;
       m_run = m_use;
       tmem_wait_st();

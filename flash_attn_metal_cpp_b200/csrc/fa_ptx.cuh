@@ -129,6 +129,32 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
+// Same as mma_ss with each descriptor given as (low word, high word): the
+// caller keeps the high words constant and advances only the start-address
+// field in the low words, so issuing an MMA costs two integer adds.
+__device__ __forceinline__ void mma_ss_lohi(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                                            uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 ad, bd;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ts_lohi(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 bd;\n\t"
+      "mov.b64 bd, {%2, %3};\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], bd, %4, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem desc]
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
@@ -265,6 +291,50 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Maximum of 128 values as a shallow tree of 3-input max instructions.
+__device__ __forceinline__ float row_max128(const float (&s)[128]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmax3f(s[i], s[i + 8], s[i + 16]);
+#pragma unroll
+  for (int k = 3; k < 15; k += 2)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmax3f(m[i], s[i + 8 * k], s[i + 8 * k + 8]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[i + 120]);
+  return fmax3f(fmax3f(m[0], m[1], m[2]), fmax3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// 2^x for two values on the FMA/ALU pipes instead of MUFU.
+// Method: Cody-Waite style range reduction x = n + f with n = round(x)
+// (adding 1.5 * 2^23 rounds to an integer), f in [-1/2, 1/2], and a degree-3
+// polynomial for 2^f whose coefficients were fitted for this build by the
+// Remez exchange algorithm on the relative error over [-1/2, 1/2]
+// (max relative error 7.5e-5, below the 2^-11 rounding of the fp16 P it
+// feeds). The result is 2^n * p(f), formed by adding n to the exponent
+// field. Inputs are clamped at -126 so the exponent never underflows.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kC0 = 0.99992807f, kC1 = 0.69326099f, kC2 = 0.24261112f, kC3 = 0.05517167f;
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 r = __fadd2_rn(x, make_float2(kRound, kRound));            // n in the low mantissa bits
+  const float2 n = __fadd2_rn(r, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);              // x - n
+  float2 p = __ffma2_rn(make_float2(kC3, kC3), f, make_float2(kC2, kC2));
+  p = __ffma2_rn(p, f, make_float2(kC1, kC1));
+  p = __ffma2_rn(p, f, make_float2(kC0, kC0));
+  // (bits(r) << 23) == n << 23: the constant's low 9 bits are zero.
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(r.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(r.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
