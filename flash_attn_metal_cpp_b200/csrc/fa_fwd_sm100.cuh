@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < NT; ++t) {
       mbar_init(smem_addr(&bars->q_full[t]), 1);
       mbar_init(smem_addr(&bars->s_full[t]), 1);
-      mbar_init(smem_addr(&bars->p_full[t]), 128);
+      mbar_init(smem_addr(&bars->p_full[t]), 4);  // one arrival per softmax warp
       mbar_init(smem_addr(&bars->o_full[t]), 1);
     }
     mbar_init(smem_addr(&bars->mma_final), 1);
@@ -396,7 +396,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       m_run = m_use;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(b_p_full);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_p_full);
     }
 
     // ---------------------------------------------------------- epilogue
