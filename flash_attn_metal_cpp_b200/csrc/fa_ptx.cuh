@@ -67,14 +67,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint (ns): the thread sleeps in hardware until
+// the phase completes or the hint elapses, instead of spinning and taking
+// issue slots from the warps that do the work.
+constexpr uint32_t kSuspendHintNs = 1000000u;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with parity `parity` of barrier `bar` has completed.
 // Returns false (and records a timeout in *status) if the limit ran out.
 __device__ __forceinline__ bool fa_wait(uint32_t bar, uint32_t parity, unsigned* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       atomicOr(status, FA_DEV_TIMEOUT);
       return false;
@@ -198,6 +213,24 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 64 consecutive columns per thread: two x32 loads and one wait in one asm statement.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&f)[64]) {
+#define FA_R8(b) "=f"(f[b]), "=f"(f[b + 1]), "=f"(f[b + 2]), "=f"(f[b + 3]), "=f"(f[b + 4]), "=f"(f[b + 5]), \
+                 "=f"(f[b + 6]), "=f"(f[b + 7])
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : FA_R8(0), FA_R8(8), FA_R8(16), FA_R8(24), FA_R8(32), FA_R8(40), FA_R8(48), FA_R8(56)
+      : "r"(taddr), "r"(taddr + 32)
+      : "memory");
+#undef FA_R8
+}
+
 // 128 consecutive columns per thread: four x32 loads issued back to back and
 // one tcgen05.wait::ld, all inside one asm statement (outputs valid after it).
 __device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&f)[128]) {
@@ -234,6 +267,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// 16 consecutive columns per thread, load and wait in one asm statement.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
       : "memory");
 }
 
@@ -310,6 +355,20 @@ __device__ __forceinline__ float row_max128(const float (&s)[128]) {
     for (int i = 0; i < 8; ++i) m[i] = fmax3f(m[i], s[i + 8 * k], s[i + 8 * k + 8]);
 #pragma unroll
   for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[i + 120]);
+  return fmax3f(fmax3f(m[0], m[1], m[2]), fmax3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
+}
+
+// Maximum of 64 values as a shallow tree of 3-input max instructions.
+__device__ __forceinline__ float row_max64(const float (&s)[64]) {
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmax3f(s[i], s[i + 8], s[i + 16]);
+#pragma unroll
+  for (int k = 3; k < 7; k += 2)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = fmax3f(m[i], s[i + 8 * k], s[i + 8 * k + 8]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = fmaxf(m[i], s[i + 56]);
   return fmax3f(fmax3f(m[0], m[1], m[2]), fmax3f(m[3], m[4], m[5]), fmaxf(m[6], m[7]));
 }
 
