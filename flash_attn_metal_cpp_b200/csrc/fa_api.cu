@@ -17,6 +17,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -133,7 +134,9 @@ struct DeviceState {
   int device = -1;
   bool ready = false;
   unsigned* status = nullptr;       // in-kernel status word
-  cudaStream_t host_stream = nullptr;
+  cudaStream_t host_stream = nullptr;   // host-pointer path: compute
+  cudaStream_t h2d_stream = nullptr;    // host-pointer path: copies in
+  cudaStream_t d2h_stream = nullptr;    // host-pointer path: copies out
   DevicePool pool;
   std::mutex mu;                    // serialises the host-pointer path and the caches
   // RoPE table cache: (theta bits, D) -> tables with `rows` rows.
@@ -189,6 +192,8 @@ fa_status device_state(DeviceState** out) {
     FA_CUDA(cudaMalloc(&ds->status, sizeof(unsigned)));
     FA_CUDA(cudaMemset(ds->status, 0, sizeof(unsigned)));
     FA_CUDA(cudaStreamCreateWithFlags(&ds->host_stream, cudaStreamNonBlocking));
+    FA_CUDA(cudaStreamCreateWithFlags(&ds->h2d_stream, cudaStreamNonBlocking));
+    FA_CUDA(cudaStreamCreateWithFlags(&ds->d2h_stream, cudaStreamNonBlocking));
     ds->device = dev;
     ds->ready = true;
   }
@@ -624,27 +629,140 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
   if ((q_bytes && !dq.p) || (k_bytes && (!dk.p || !dv.p)) || (o_bytes && !dout.p) || (lse && lse_bytes && !dl.p) ||
       (tables && tab_bytes && (!dc.p || !dsn.p)) || (pl.ws_bytes && !dws.p))
     return fail(FA_ERR_CUDA, "device allocation failed");
-  if (q_bytes) FA_CUDA(cudaMemcpyAsync(dq.p, q, q_bytes, cudaMemcpyHostToDevice, s));
-  if (k_bytes) {
-    FA_CUDA(cudaMemcpyAsync(dk.p, k, k_bytes, cudaMemcpyHostToDevice, s));
-    FA_CUDA(cudaMemcpyAsync(dv.p, v, k_bytes, cudaMemcpyHostToDevice, s));
-  }
   if (tables && tab_bytes) {
     FA_CUDA(cudaMemcpyAsync(dc.p, cos, tab_bytes, cudaMemcpyHostToDevice, s));
     FA_CUDA(cudaMemcpyAsync(dsn.p, sin, tab_bytes, cudaMemcpyHostToDevice, s));
   }
-  pl.a.o = dout.p;
-  pl.a.lse = static_cast<float*>(dl.p);
-  st = run(pl, dq.p ? dq.p : (const void*)1, dk.p ? dk.p : (const void*)1, dv.p ? dv.p : (const void*)1,
-           tables ? static_cast<const float*>(dc.p) : nullptr, tables ? static_cast<const float*>(dsn.p) : nullptr,
-           dws.p, pl.ws_bytes, s, ds);
-  if (st != FA_OK) {
-    cudaStreamSynchronize(s);
-    return st;
+  const float* tc = tables ? static_cast<const float*>(dc.p) : nullptr;
+  const float* tsn = tables ? static_cast<const float*>(dsn.p) : nullptr;
+
+  // Independent chunks: whole batches, or (batch 1) groups of KV heads with
+  // their query heads. Chunk c's copy in, compute and copy out run on three
+  // streams ordered by events, so transfers overlap the attention kernels.
+  struct Chunk { int b0, nb, hk0, nhk; };
+  std::vector<Chunk> chunks;
+  const int kMaxChunks = 8;
+  const bool small = q_bytes + 2 * k_bytes < (size_t(16) << 20);
+  if (!small && a.B >= 2) {
+    const int per = (a.B + kMaxChunks - 1) / kMaxChunks;
+    for (int b0 = 0; b0 < a.B; b0 += per) chunks.push_back({b0, std::min(per, a.B - b0), 0, a.Hk});
+  } else if (!small && a.B == 1 && a.Hk >= 2) {
+    const int n = std::min(a.Hk, kMaxChunks);
+    const int per = (a.Hk + n - 1) / n;
+    for (int h0 = 0; h0 < a.Hk; h0 += per) chunks.push_back({0, 1, h0, std::min(per, a.Hk - h0)});
   }
-  if (o_bytes) FA_CUDA(cudaMemcpyAsync(o, dout.p, o_bytes, cudaMemcpyDeviceToHost, s));
-  if (lse && lse_bytes) FA_CUDA(cudaMemcpyAsync(lse, dl.p, lse_bytes, cudaMemcpyDeviceToHost, s));
-  FA_CUDA(cudaStreamSynchronize(s));
+  if (chunks.size() <= 1 || q_bytes == 0 || k_bytes == 0) {
+    // One piece: copy in, run, copy out on one stream.
+    if (q_bytes) FA_CUDA(cudaMemcpyAsync(dq.p, q, q_bytes, cudaMemcpyHostToDevice, s));
+    if (k_bytes) {
+      FA_CUDA(cudaMemcpyAsync(dk.p, k, k_bytes, cudaMemcpyHostToDevice, s));
+      FA_CUDA(cudaMemcpyAsync(dv.p, v, k_bytes, cudaMemcpyHostToDevice, s));
+    }
+    pl.a.o = dout.p;
+    pl.a.lse = static_cast<float*>(dl.p);
+    st = run(pl, dq.p ? dq.p : (const void*)1, dk.p ? dk.p : (const void*)1, dv.p ? dv.p : (const void*)1, tc,
+             tsn, dws.p, pl.ws_bytes, s, ds);
+    if (st != FA_OK) {
+      cudaStreamSynchronize(s);
+      return st;
+    }
+    if (o_bytes) FA_CUDA(cudaMemcpyAsync(o, dout.p, o_bytes, cudaMemcpyDeviceToHost, s));
+    if (lse && lse_bytes) FA_CUDA(cudaMemcpyAsync(lse, dl.p, lse_bytes, cudaMemcpyDeviceToHost, s));
+    FA_CUDA(cudaStreamSynchronize(s));
+    return fa_check_device_status();
+  }
+
+  cudaStream_t s_in = ds->h2d_stream, s_out = ds->d2h_stream;
+  auto sync_all = [&]() {
+    cudaStreamSynchronize(s_in);
+    cudaStreamSynchronize(s);
+    cudaStreamSynchronize(s_out);
+  };
+  // The copies of the tables above were queued on `s`; the copy stream waits for them too.
+  cudaEvent_t ev_tab;
+  FA_CUDA(cudaEventCreateWithFlags(&ev_tab, cudaEventDisableTiming));
+  FA_CUDA(cudaEventRecord(ev_tab, s));
+  FA_CUDA(cudaStreamWaitEvent(s_in, ev_tab, 0));
+  cudaEventDestroy(ev_tab);
+  std::vector<cudaEvent_t> ev_in(chunks.size()), ev_done(chunks.size());
+  for (size_t c = 0; c < chunks.size(); ++c) {
+    FA_CUDA(cudaEventCreateWithFlags(&ev_in[c], cudaEventDisableTiming));
+    FA_CUDA(cudaEventCreateWithFlags(&ev_done[c], cudaEventDisableTiming));
+  }
+  auto destroy_events = [&]() {
+    for (size_t c = 0; c < chunks.size(); ++c) {
+      cudaEventDestroy(ev_in[c]);
+      cudaEventDestroy(ev_done[c]);
+    }
+  };
+  // Copy `rows` rows of `width` bytes between tensors with `pitch`-byte rows.
+  auto copy_rows = [](void* dst, const void* src, size_t width, size_t pitch, size_t rows, cudaMemcpyKind kind,
+                      cudaStream_t st) -> cudaError_t {
+    if (width == pitch) return cudaMemcpyAsync(dst, src, width * rows, kind, st);
+    return cudaMemcpy2DAsync(dst, pitch, src, pitch, width, rows, kind, st);
+  };
+  const int group = a.group;
+  st = FA_OK;
+  for (size_t c = 0; c < chunks.size() && st == FA_OK; ++c) {
+    const Chunk& ch = chunks[c];
+    const int hq0 = ch.hk0 * group, nhq = ch.nhk * group;
+    const size_t q_off = ((size_t)ch.b0 * a.Sq * a.Hq + hq0) * a.D;   // elements
+    const size_t k_off = ((size_t)ch.b0 * a.Sk * a.Hk + ch.hk0) * a.D;
+    const size_t q_rows = (size_t)ch.nb * a.Sq, k_rows = (size_t)ch.nb * a.Sk;
+    const size_t q_pitch = (size_t)a.Hq * a.D, k_pitch = (size_t)a.Hk * a.D;
+    const bool full_heads = (ch.nhk == a.Hk);
+    // copy in
+    cudaError_t e = copy_rows(static_cast<char*>(dq.p) + q_off * in_sz, static_cast<const char*>(q) + q_off * in_sz,
+                              (full_heads ? q_pitch * a.Sq * ch.nb : (size_t)nhq * a.D) * in_sz,
+                              (full_heads ? q_pitch * a.Sq * ch.nb : q_pitch) * in_sz, full_heads ? 1 : q_rows,
+                              cudaMemcpyHostToDevice, s_in);
+    for (int m = 0; m < 2 && e == cudaSuccess; ++m)
+      e = copy_rows(static_cast<char*>(m ? dv.p : dk.p) + k_off * in_sz,
+                    static_cast<const char*>(m ? v : k) + k_off * in_sz,
+                    (full_heads ? k_pitch * a.Sk * ch.nb : (size_t)ch.nhk * a.D) * in_sz,
+                    (full_heads ? k_pitch * a.Sk * ch.nb : k_pitch) * in_sz, full_heads ? 1 : k_rows,
+                    cudaMemcpyHostToDevice, s_in);
+    if (e == cudaSuccess) e = cudaEventRecord(ev_in[c], s_in);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev_in[c], 0);
+    if (e != cudaSuccess) {
+      st = cuda_fail(e, "chunk copy in");
+      break;
+    }
+    // compute: the chunk as its own problem over strided views of the full buffers
+    Plan sub = pl;
+    sub.a.B = ch.nb;
+    sub.a.Hq = nhq;
+    sub.a.Hk = ch.nhk;
+    sub.ws_bytes = 0;
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    if (sub.need_q16) sub.ws_bytes += up((size_t)ch.nb * a.Sq * nhq * a.D * 2);
+    if (sub.need_k16) sub.ws_bytes += up((size_t)ch.nb * a.Sk * ch.nhk * a.D * 2);
+    if (sub.need_v16) sub.ws_bytes += up((size_t)ch.nb * a.Sk * ch.nhk * a.D * 2);
+    sub.a.o = static_cast<char*>(dout.p) + q_off * out_sz;
+    sub.a.lse = dl.p ? static_cast<float*>(dl.p) + ((size_t)ch.b0 * a.Hq + hq0) * a.Sq : nullptr;
+    st = run(sub, static_cast<const char*>(dq.p) + q_off * in_sz, static_cast<const char*>(dk.p) + k_off * in_sz,
+             static_cast<const char*>(dv.p) + k_off * in_sz, tc, tsn, dws.p, pl.ws_bytes, s, ds);
+    if (st != FA_OK) break;
+    e = cudaEventRecord(ev_done[c], s);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev_done[c], 0);
+    // copy out
+    if (e == cudaSuccess)
+      e = copy_rows(static_cast<char*>(o) + q_off * out_sz, static_cast<const char*>(dout.p) + q_off * out_sz,
+                    (full_heads ? q_pitch * a.Sq * ch.nb : (size_t)nhq * a.D) * out_sz,
+                    (full_heads ? q_pitch * a.Sq * ch.nb : q_pitch) * out_sz, full_heads ? 1 : q_rows,
+                    cudaMemcpyDeviceToHost, s_out);
+    if (e == cudaSuccess && lse) {
+      const size_t l_off = ((size_t)ch.b0 * a.Hq + hq0) * a.Sq;
+      e = cudaMemcpyAsync(lse + l_off, static_cast<const float*>(dl.p) + l_off,
+                          (size_t)ch.nb * nhq * a.Sq * sizeof(float), cudaMemcpyDeviceToHost, s_out);
+    }
+    if (e != cudaSuccess) st = cuda_fail(e, "chunk copy out");
+  }
+  sync_all();
+  destroy_events();
+  if (st != FA_OK) return st;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "pipelined host path");
   return fa_check_device_status();
 }
 

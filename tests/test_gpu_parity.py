@@ -305,3 +305,25 @@ def test_repeated_calls_deterministic(fa, cuda_device):
     a = fa.forward(q, k, v, softmax_scale=0.1, is_causal=True, rope_theta=1e4)
     b = fa.forward(q, k, v, softmax_scale=0.1, is_causal=True, rope_theta=1e4)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,S,Hq,Hk,dtype,theta", [(3, 4096, 8, 2, "bfloat16", 5e5), (1, 8192, 8, 4, "float16", None),
+                                                  (1, 6000, 6, 3, "bfloat16", 1e4)])
+def test_host_path_chunked_pipeline_matches_device_path(fa, cuda_device, B, S, Hq, Hk, dtype, theta):
+    """Large host-pointer calls are split into batch / KV-head-group chunks whose
+    copies overlap compute; every chunk must equal the device-path result."""
+    import torch
+
+    tdt = _torch_dtype(dtype)
+    q, k, v = _inputs((B, S, Hq, 128), (B, S, Hk, 128), tdt, seed=B * S + Hq)
+    kw = {"rope_theta": theta} if theta else {}
+    ref, ref_lse = fa.forward(q, k, v, softmax_scale=0.09, is_causal=True, return_lse=True, **kw)
+    qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
+    out, lse = fa.forward(qh, kh, vh, softmax_scale=0.09, is_causal=True, return_lse=True, **kw)
+    assert not out.is_cuda
+    torch.testing.assert_close(out, ref.cpu(), rtol=0, atol=0)
+    torch.testing.assert_close(lse, ref_lse.cpu(), rtol=0, atol=0)
+    # pageable NumPy arrays take the same path
+    if dtype == "float16":
+        out_np = fa.forward(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), softmax_scale=0.09, is_causal=True, **kw)
+        assert np.array_equal(out_np, ref.cpu().numpy())
