@@ -27,6 +27,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# Rank 0's stdout carries exactly one JSON line: keep NCCL's banner off it.
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 METRIC = "attn fwd TFLOP/s and % of B200 dense BF16 peak at 1/2/4/8 GPUs; ms/call"
 DATASHEET_BF16_TFLOPS = 2250.0
@@ -147,9 +149,11 @@ def cpu_sample(cfg, budget_s=12.0, max_heads=64):
     from oracle import attention_oracle as orc
 
     B, S, Hq, Hkv, D, dt, causal, theta, amp, _ = cfg
+    # All host cores, also under torchrun (which sets OMP_NUM_THREADS=1).
     try:
-        from threadpoolctl import threadpool_info
+        from threadpoolctl import threadpool_info, threadpool_limits
 
+        threadpool_limits(limits=os.cpu_count())
         cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
     except Exception:  # pragma: no cover
         cores = os.cpu_count()
