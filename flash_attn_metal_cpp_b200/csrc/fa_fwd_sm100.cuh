@@ -72,7 +72,7 @@ struct Cfg {
 struct Bars {
   uint64_t q_full[NT];
   uint64_t s_full[NT];
-  uint64_t p_full[NT];
+  uint64_t p_full[NT][2];    // P of keys [0, 64) and [64, 128) written to TMEM
   uint64_t o_full[NT];
   uint64_t mma_final;
   uint64_t k_full[4];
@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < NT; ++t) {
       mbar_init(smem_addr(&bars->q_full[t]), 1);
       mbar_init(smem_addr(&bars->s_full[t]), 1);
-      mbar_init(smem_addr(&bars->p_full[t]), 4);  // one arrival per softmax warp
+      mbar_init(smem_addr(&bars->p_full[t][0]), 4);  // one arrival per softmax warp
+      mbar_init(smem_addr(&bars->p_full[t][1]), 4);
       mbar_init(smem_addr(&bars->o_full[t]), 1);
     }
     mbar_init(smem_addr(&bars->mma_final), 1);
@@ -268,13 +269,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!fa_wait(smem_addr(&bars->v_full[i % C::NS]), (i / C::NS) & 1, a.status)) { ok = false; break; }
               v_ready = true;
             }
-            if (!fa_wait(smem_addr(&bars->p_full[t]), i & 1, a.status)) { ok = false; break; }
-            tc_fence_after();
             // 16 keys x D cols per MMA: D-halves C::BOX_BYTES apart (LBO), 8-key groups 1024 B (SBO).
+            // The first 64 keys go as soon as their P is written, while the
+            // softmax still computes the second half.
             const uint32_t v_lo = v_lo0 + (uint32_t)((i % C::NS) * C::TILE_BYTES >> 4);
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk)
-              mma_ts_lohi(tO, tS + kk * 8, v_lo + kk * (16 * 128 >> 4), v_hi, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            for (int half = 0; half < 2; ++half) {
+              if (!fa_wait(smem_addr(&bars->p_full[t][half]), i & 1, a.status)) { ok = false; break; }
+              tc_fence_after();
+#pragma unroll
+              for (int kk = half * 4; kk < half * 4 + 4; ++kk)
+                mma_ts_lohi(tO, tS + kk * 8, v_lo + kk * (16 * 128 >> 4), v_hi, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+            }
+            if (!ok) break;
             if (i == n_kv_t[t] - 1) mma_commit(smem_addr(&bars->o_full[t]));
           }
           if (j < n_kv_t[t]) {
@@ -314,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tS = lane_base + kColS + t * 128;
     const uint32_t tO = lane_base + kColO + t * 128;
     const uint32_t b_s_full = smem_addr(&bars->s_full[t]);
-    const uint32_t b_p_full = smem_addr(&bars->p_full[t]);
+    const uint32_t b_p_full = smem_addr(&bars->p_full[t][0]);  // [t][1] is 8 bytes further
     const float sl2 = a.scale_log2;
     float m_run = -INFINITY;  // running max in log2 units (value actually subtracted)
     float l_run = 0.f;
@@ -390,6 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         tmem_st16(tS + c0 / 2, p);  // P columns [c0/2, c0/2+16) of S_t's region
+        if (c0 == 32) {  // keys [0, 64) done: let the first half of PV start
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(b_p_full);
+        }
       }
       const float rsum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
       l_run = l_run * alpha + rsum;
@@ -397,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b_p_full);
+      if (lane == 0) mbar_arrive(b_p_full + 8);  // p_full[t][1]
     }
 
     // ---------------------------------------------------------- epilogue
