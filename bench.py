@@ -6,7 +6,11 @@ rotate-half RoPE theta=5e5, seeded N(0,1) inputs resident in HBM. A step is
 one `_flash_attn_metal.forward` call (RoPE/convert pre-pass + attention
 kernel). With --gpus N (torchrun, one process per GPU) every rank runs its
 own batch shard of that size (weak scaling, no collective on the data path);
-value = FLOPs of all ranks / max-over-ranks device time.
+value = FLOPs of all ranks / max-over-ranks device time. cfg5b (8 query
+heads over one KV head) instead splits ONE problem across the ranks by key
+range (strong scaling): a step is the partial kernel with its epilogue
+storing into the row owners' staging over NVLink, a one-element NCCL
+barrier, and the owners' merge.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4]
     python bench.py --impl reference ...   # the oracle port on the host cores
@@ -43,7 +47,13 @@ CONFIGS = {
              "causal GQA bf16 B4 S8192 Hq32 Hkv8 D128 RoPE 5e5"),
     "cfg5a": (1, 65536, 64, 8, 128, "bfloat16", True, 500000.0, 0.5,
               "long-context causal GQA bf16 B1 S65536 Hq64 Hkv8 D128 RoPE 5e5"),
+    "cfg5b": (1, 65536, 8, 1, 128, "bfloat16", True, 500000.0, 0.5,
+              "long-context causal MQA bf16 B1 S65536 Hq8 Hkv1 D128 RoPE 5e5 (split-KV across GPUs)"),
 }
+# Configs whose one problem is split across the ranks (strong scaling):
+# balanced key ranges per rank, partials stored into the row owners' staging
+# over NVLink, merged by the owners.
+SPLIT_KV = {"cfg5b"}
 
 
 def flops(B, S, Hq, D, causal):
@@ -212,6 +222,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
+    ap.add_argument("--split", choices=["kv", "q"], default="kv",
+                    help="how cfg5b is split over ranks: key ranges + merge (kv) or zig-zag query rows (q)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -244,12 +256,38 @@ def main():
 
     B, S, Hq, Hkv, D, dt, causal, theta, amp, desc = cfg
     scale = 1.0 / math.sqrt(D) if args.config != "cfg1" else 0.125
-    q, k, v = make_inputs(cfg, device, seed=1234 + rank)
-    out = torch.empty((B, S, Hq, D), dtype=q.dtype, device=device)
+    shared = args.config in SPLIT_KV and world > 1  # one problem over all ranks
+    split_kv = shared and args.split == "kv"
+    # Ranks sharing one problem use the same seed.
+    q, k, v = make_inputs(cfg, device, seed=1234 + (0 if args.config in SPLIT_KV else rank))
     kw = {"rope_theta": theta} if theta else {}
+    att = qs = None
+    if split_kv:
+        from flash_attn_metal_cpp_b200.multi_gpu import SplitKVAttention
 
-    def step():
-        fa.forward(q, k, v, softmax_scale=scale, is_causal=causal, out=out, **kw)
+        att = SplitKVAttention(B, S, S, Hq, Hkv, D, causal)
+        blo, bhi = att.plan.owner_block(rank)
+        out = torch.empty((B, bhi - blo, Hq, D), dtype=q.dtype, device=device)
+        share = att.plan.pair_work(rank) / max(1, sum(att.plan.pair_work(r) for r in range(world)))
+
+        def step():
+            att.forward(q, k, v, scale, out=out, **kw)
+    elif shared:
+        from flash_attn_metal_cpp_b200.multi_gpu import QShardAttention
+
+        qs = QShardAttention(S, rank, world, device)
+        out = torch.empty((B, S, Hq, D), dtype=q.dtype, device=device)
+        rows_work = sum((hi * (hi + 1) - lo * (lo + 1)) // 2 if causal else (hi - lo) * S for lo, hi in qs.ranges)
+        share = rows_work / ((S * (S + 1)) // 2 if causal else S * S)
+
+        def step():
+            qs.forward(q, k, v, scale, causal, out, **kw)
+    else:
+        out = torch.empty((B, S, Hq, D), dtype=q.dtype, device=device)
+        share = 1.0
+
+        def step():
+            fa.forward(q, k, v, softmax_scale=scale, is_causal=causal, out=out, **kw)
 
     for _ in range(args.warmup):
         step()
@@ -285,18 +323,55 @@ def main():
     max_ms = float(t.item())
 
     f_step = flops(B, S, Hq, D, causal)
-    value = f_step * world * args.steps / (max_ms / 1e3) / 1e12
+    f_job = f_step if shared else f_step * world  # shared: one problem over all ranks
+    value = f_job * args.steps / (max_ms / 1e3) / 1e12
     ms_per_step = max_ms / args.steps
 
     # End to end through the public API with pinned host buffers: every step
     # copies Q/K/V host->device, runs, and copies O device->host.
     e2e = None
     if args.e2e_steps > 0:
-        qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
-        oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        if split_kv:
+            # Each rank copies in the query rows and the key range its share
+            # reads, and copies out the rows it owns.
+            qlo, _ = att.plan.q_ranges[rank]
+            klo, khi = att.plan.kv_ranges[rank]
+            qh = q[:, qlo:].cpu().pin_memory()
+            kh, vh = (x[:, klo:khi].cpu().pin_memory() for x in (k, v))
+            oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+            h2d_rank = sum(x.numel() * x.element_size() for x in (qh, kh, vh))
 
-        def e2e_step():
-            fa.forward(qh, kh, vh, softmax_scale=scale, is_causal=causal, out=oh, **kw)
+            def e2e_step():
+                q[:, qlo:].copy_(qh, non_blocking=True)
+                k[:, klo:khi].copy_(kh, non_blocking=True)
+                v[:, klo:khi].copy_(vh, non_blocking=True)
+                att.forward(q, k, v, scale, out=out, **kw)
+                oh.copy_(out, non_blocking=True)
+                torch.cuda.current_stream(device).synchronize()
+        elif shared:
+            # Query rows of the rank's two chunks in, keys up to its last row in, its rows out.
+            kv_hi = max(hi for _, hi in qs.ranges) if causal else S
+            qhs = [q[:, lo:hi].cpu().pin_memory() for lo, hi in qs.ranges]
+            kh, vh = (x[:, :kv_hi].cpu().pin_memory() for x in (k, v))
+            ohs = [torch.empty(x.shape, dtype=out.dtype).pin_memory() for x in qhs]
+            h2d_rank = sum(x.numel() * x.element_size() for x in qhs + [kh, vh])
+
+            def e2e_step():
+                for (lo, hi), x in zip(qs.ranges, qhs):
+                    q[:, lo:hi].copy_(x, non_blocking=True)
+                k[:, :kv_hi].copy_(kh, non_blocking=True)
+                v[:, :kv_hi].copy_(vh, non_blocking=True)
+                qs.forward(q, k, v, scale, causal, out, **kw)
+                for (lo, hi), x in zip(qs.ranges, ohs):
+                    x.copy_(out[:, lo:hi], non_blocking=True)
+                torch.cuda.current_stream(device).synchronize()
+        else:
+            qh, kh, vh = (x.cpu().pin_memory() for x in (q, k, v))
+            oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+            h2d_rank = sum(x.numel() * x.element_size() for x in (q, k, v))
+
+            def e2e_step():
+                fa.forward(qh, kh, vh, softmax_scale=scale, is_causal=causal, out=oh, **kw)
 
         e2e_step()
         if dist:
@@ -307,14 +382,26 @@ def main():
         e2e_s = torch.tensor([(time.perf_counter() - t0) / args.e2e_steps], dtype=torch.float64, device=device)
         if dist:
             dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-        h2d = sum(x.numel() * x.element_size() for x in (q, k, v))
-        e2e = {"value": f_step * world / float(e2e_s.item()) / 1e12, "unit": "TFLOP/s",
+        d2h_rank = sum(x.numel() * x.element_size() for x in ohs) if (shared and not split_kv) else \
+            out.numel() * out.element_size()
+        h2d = torch.tensor([h2d_rank, d2h_rank], dtype=torch.float64, device=device)
+        if dist:
+            dist.all_reduce(h2d)
+        e2e = {"value": f_job / float(e2e_s.item()) / 1e12, "unit": "TFLOP/s",
                "ms_per_step": float(e2e_s.item()) * 1e3,
-               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": out.numel() * out.element_size() * world}
+               "h2d_bytes_per_step": int(h2d[0].item()), "d2h_bytes_per_step": int(h2d[1].item())}
 
     peaks, peak_kind = load_peaks()
     kern_avg_ms = kern_ms / max(kern_launches, 1)
-    achieved = f_step / (kern_avg_ms / 1e3) / 1e12 if kern_launches else None
+    if shared and not split_kv:
+        # Two concurrent launches per step: time the pair by the step itself.
+        kern_avg_ms = elapsed_ms / args.steps
+    kern_ranks = torch.zeros(world, dtype=torch.float64, device=device)
+    kern_ranks[rank] = kern_avg_ms
+    if dist:
+        dist.all_reduce(kern_ranks)
+    # FLOPs of this rank's launches (its share of the problem under split-KV).
+    achieved = f_step * share / (kern_avg_ms / 1e3) / 1e12 if kern_launches else None
     long_region = max_ms > 1000.0
     peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
     traffic = load_traffic(args.config)
@@ -322,6 +409,7 @@ def main():
         "bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
         "frac": (achieved / peak) if achieved else None, "traffic": traffic,
         "kernel": "attn_fwd_sm100 (tcgen05)", "kernel_ms_avg": kern_avg_ms,
+        "kernel_ms_per_rank": [round(float(x), 4) for x in kern_ranks.tolist()],
         "peak_source": f"{peak_kind} {'sustained' if long_region else 'burst'} bf16 GEMM",
         "frac_of_datasheet_2250": (achieved / DATASHEET_BF16_TFLOPS) if achieved else None,
     }
@@ -335,14 +423,21 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if args.config in SPLIT_KV else "weak",
             "vs_baseline": None, "dtype": {"float32": "f32", "float16": "fp16", "bfloat16": "bf16"}[dt],
-            "data": "synthetic (seeded N(0,1) per rank)",
+            "data": "synthetic (seeded N(0,1); one problem shared by all ranks)" if args.config in SPLIT_KV
+                    else "synthetic (seeded N(0,1) per rank)",
             "config": {
-                "workload": args.config + ": " + desc, "batch_per_gpu": B, "global_batch": B * world,
+                "workload": args.config + ": " + desc, "batch_per_gpu": None if shared else B,
+                "global_batch": B if args.config in SPLIT_KV else B * world,
                 "seq_len": S, "heads_q": Hq, "heads_kv": Hkv, "head_dim": D, "causal": causal,
-                "rope_theta": theta, "softmax_scale": scale, "parallelism": f"batch shard x{world}",
-                "flops_per_step_per_gpu": f_step,
+                "rope_theta": theta, "softmax_scale": scale,
+                "parallelism": (f"split-KV x{world} (key ranges {att.plan.kv_ranges}, owner rows "
+                                f"{att.plan.owner_rows})") if split_kv else
+                               (f"zig-zag query rows x{world} (K/V replicated, no merge)" if shared
+                                else f"batch shard x{world}"),
+                "flops_per_step_per_gpu": f_step * share if shared else f_step,
                 "l2": "inputs + output {:.0f} MB > 126 MB L2 (no flush)".format(
                     sum(x.numel() * x.element_size() for x in (q, k, v, out)) / 1e6),
                 "mma_operands": "fp16 for bf16 inputs (converted in the RoPE pre-pass), fp32 accumulate",
@@ -356,6 +451,8 @@ def main():
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if att is not None:
+        att.close()
     if dist:
         dist.barrier()
         dist.destroy_process_group()

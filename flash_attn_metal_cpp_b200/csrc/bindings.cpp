@@ -29,7 +29,9 @@ namespace py = pybind11;
 
 namespace {
 
-int g_device = 0;
+// initialize / get_device_info act on the calling thread's current CUDA
+// device (device 0 unless the caller selected another, e.g. one per rank).
+constexpr int g_device = -1;
 
 std::string err_text(fa_status st) {
   std::string s = fa_last_error();
@@ -288,6 +290,184 @@ py::object forward_torch(py::object Q, py::object K, py::object V, float scale, 
   return out;
 }
 
+// ------------------------------------------ range / combine / IPC (torch CUDA)
+template <typename T>
+T* tptr(const py::object& t) {
+  return reinterpret_cast<T*>(t.attr("data_ptr")().cast<uintptr_t>());
+}
+
+void* current_stream_of(const py::object& t) {
+  py::module_ torch = py::module_::import("torch");
+  return reinterpret_cast<void*>(
+      torch.attr("cuda").attr("current_stream")(t.attr("device")).attr("cuda_stream").cast<uintptr_t>());
+}
+
+void require_cuda(const py::object& t, const char* name) {
+  if (!is_torch_tensor(t) || !t.attr("is_cuda").cast<bool>())
+    forward_error(std::string(name) + " must be a CUDA torch tensor");
+}
+
+// Rows [q_begin, q_end) against keys [kv_begin, kv_end): writes out / lse,
+// or the owners' slots listed in `route` (int64 CUDA tensor of 2*n_owners
+// addresses) when given.
+void py_forward_range(py::object Q, py::object K, py::object V, std::pair<int64_t, int64_t> q_range,
+                      std::pair<int64_t, int64_t> kv_range, py::object out, py::object lse,
+                      float softmax_scale, bool is_causal, py::object cos, py::object sin,
+                      py::object rope_theta, py::object out_dtype, py::object route, int n_owners,
+                      int64_t owner_rows) {
+  require_cuda(Q, "Q");
+  require_cuda(K, "K");
+  require_cuda(V, "V");
+  const int code = dtype_code_from_name(py::str(Q.attr("dtype")));
+  if (code < 0 || dtype_code_from_name(py::str(K.attr("dtype"))) != code ||
+      dtype_code_from_name(py::str(V.attr("dtype"))) != code)
+    forward_error("Input tensors must be float16, bfloat16 or float32, all of one dtype");
+  std::vector<int64_t> qs = tsize(Q), ks = tsize(K), vs = tsize(V);
+  check_shapes(qs, ks, vs);
+  const bool rotary_tables = !cos.is_none() && !sin.is_none();
+  const float theta = rope_theta.is_none() ? 0.f : rope_theta.cast<float>();
+  fa_params p;
+  fill_params(p, qs, ks, softmax_scale, is_causal, 0.f, py::none(), py::none(), rotary_tables || theta > 0.f,
+              theta);
+  p.dtype = code;
+  p.out_dtype = parse_out_dtype(out_dtype);
+  const int oc = p.out_dtype < 0 ? code : p.out_dtype;
+  py::object q = inner_contig(Q), k = inner_contig(K), v = inner_contig(V);
+  auto qst = tstride(q), kst = tstride(k), vst = tstride(v);
+  for (int i = 0; i < 3; ++i) {
+    p.q_stride[i] = qst[i];
+    p.k_stride[i] = kst[i];
+    p.v_stride[i] = vst[i];
+  }
+  const py::object dev = Q.attr("device");
+  const int dev_index = dev.attr("index").is_none() ? 0 : dev.attr("index").cast<int>();
+  fa_status st = fa_init(dev_index);
+  if (st != FA_OK) forward_error(err_text(st));
+  void* op = nullptr;
+  float* lp = nullptr;
+  fa_route rt{};
+  if (!route.is_none()) {
+    require_cuda(route, "route");
+    if (route.attr("numel")().cast<int64_t>() != 2 * (int64_t)n_owners)
+      forward_error("route must hold 2 * n_owners addresses");
+    rt.table = tptr<const uint64_t>(route);
+    rt.n_owners = n_owners;
+    rt.owner_rows = (uint32_t)owner_rows;
+  } else {
+    require_cuda(out, "out");
+    if (tsize(out) != qs) forward_error("out has the wrong shape");
+    if (dtype_code_from_name(py::str(out.attr("dtype"))) != oc) forward_error("out has the wrong dtype");
+    auto ost = tstride(out);
+    if (ost[3] != 1) forward_error("out needs a unit innermost stride");
+    for (int i = 0; i < 3; ++i) p.o_stride[i] = ost[i];
+    op = tptr<void>(out);
+    if (!lse.is_none()) {
+      require_cuda(lse, "lse");
+      if (tsize(lse) != std::vector<int64_t>{qs[0], qs[2], qs[1]} ||
+          !lse.attr("is_contiguous")().cast<bool>() ||
+          dtype_code_from_name(py::str(lse.attr("dtype"))) != FA_F32)
+        forward_error("lse must be a contiguous float32 [batch, num_heads_q, seqlen_q] tensor");
+      lp = tptr<float>(lse);
+    }
+  }
+  py::object ct = py::none(), stt = py::none();
+  const float* cp = nullptr;
+  const float* sp = nullptr;
+  if (rotary_tables) {
+    py::module_ torch = py::module_::import("torch");
+    ct = torch.attr("as_tensor")(cos, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    stt = torch.attr("as_tensor")(sin, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    const int64_t need = std::max(qs[1], ks[1]) * (qs[3] / 2);
+    if (ct.attr("numel")().cast<int64_t>() < need || stt.attr("numel")().cast<int64_t>() < need)
+      forward_error("cos/sin tables must hold [max(seqlen_q, seqlen_k), head_dim/2] float32 values");
+    cp = tptr<const float>(ct);
+    sp = tptr<const float>(stt);
+  }
+  if (q_range.first < 0 || kv_range.first < 0) forward_error("ranges must be non-negative");
+  st = fa_forward_range(&p, tptr<const void>(q), tptr<const void>(k), tptr<const void>(v), op, lp, cp, sp,
+                        (uint32_t)q_range.first, (uint32_t)q_range.second, (uint32_t)kv_range.first,
+                        (uint32_t)kv_range.second, route.is_none() ? nullptr : &rt, nullptr, 0,
+                        current_stream_of(Q));
+  if (st != FA_OK) forward_error(err_text(st));
+}
+
+// Merge n split partials: o_parts [n, B, Sq, Hq, D] and lse_parts
+// [n, B, Hq, Sq] (float32, contiguous) into rows q_range of out
+// [B, >= q_range end, Hq, D] (any of the three dtypes, unit innermost
+// stride) and optionally lse [B, Hq, Sq].
+void py_combine(py::object o_parts, py::object lse_parts, py::object out, py::object lse,
+                py::object q_range) {
+  require_cuda(o_parts, "o_parts");
+  require_cuda(lse_parts, "lse_parts");
+  require_cuda(out, "out");
+  std::vector<int64_t> os = tsize(o_parts), ls = tsize(lse_parts), outs = tsize(out);
+  if (os.size() != 5 || ls.size() != 4 || outs.size() != 4)
+    forward_error("o_parts must be [n, B, Sq, Hq, D], lse_parts [n, B, Hq, Sq], out [B, Sq, Hq, D]");
+  int64_t q0 = 0, q1 = os[2];
+  if (!q_range.is_none()) {
+    auto r = q_range.cast<std::pair<int64_t, int64_t>>();
+    q0 = r.first;
+    q1 = r.second;
+  }
+  if (q0 < 0 || q1 < q0 || q1 > os[2]) forward_error("bad q_range");
+  // out may have fewer rows than the staging (a ragged last block) as long
+  // as it holds the merged range.
+  if (ls != std::vector<int64_t>{os[0], os[1], os[3], os[2]} || outs[0] != os[1] || outs[1] < q1 ||
+      outs[2] != os[3] || outs[3] != os[4])
+    forward_error("o_parts, lse_parts and out disagree in shape");
+  if (!o_parts.attr("is_contiguous")().cast<bool>() || !lse_parts.attr("is_contiguous")().cast<bool>() ||
+      dtype_code_from_name(py::str(o_parts.attr("dtype"))) != FA_F32 ||
+      dtype_code_from_name(py::str(lse_parts.attr("dtype"))) != FA_F32)
+    forward_error("o_parts and lse_parts must be contiguous float32");
+  const int oc = dtype_code_from_name(py::str(out.attr("dtype")));
+  if (oc < 0) forward_error("out must be float16, bfloat16 or float32");
+  auto ost = tstride(out);
+  if (ost[3] != 1) forward_error("out needs a unit innermost stride");
+  fa_params p;
+  fa_params_init(&p);
+  p.batch_size = (uint32_t)os[1];
+  p.seqlen_q = (uint32_t)os[2];
+  p.seqlen_k = 1;
+  p.num_heads_q = p.num_heads_k = (uint32_t)os[3];
+  p.head_dim = (uint32_t)os[4];
+  p.dtype = FA_F32;
+  p.out_dtype = oc;
+  for (int i = 0; i < 3; ++i) p.o_stride[i] = ost[i];
+  float* lp = nullptr;
+  if (!lse.is_none()) {
+    require_cuda(lse, "lse");
+    if (tsize(lse) != std::vector<int64_t>{os[1], os[3], os[2]} || !lse.attr("is_contiguous")().cast<bool>())
+      forward_error("lse must be a contiguous float32 [B, Hq, Sq] tensor");
+    lp = tptr<float>(lse);
+  }
+  const py::object dev = out.attr("device");
+  fa_status st = fa_init(dev.attr("index").is_none() ? 0 : dev.attr("index").cast<int>());
+  if (st != FA_OK) forward_error(err_text(st));
+  st = fa_combine(&p, tptr<const float>(o_parts), tptr<const float>(lse_parts), (int32_t)os[0], tptr<void>(out),
+                  lp, (uint32_t)q0, (uint32_t)q1, current_stream_of(out));
+  if (st != FA_OK) forward_error(err_text(st));
+}
+
+py::tuple py_ipc_alloc(size_t bytes) {
+  void* p = nullptr;
+  fa_ipc_handle h;
+  fa_status st = fa_ipc_alloc(bytes, &p, &h);
+  if (st != FA_OK) throw std::runtime_error(err_text(st));
+  return py::make_tuple(reinterpret_cast<uintptr_t>(p),
+                        py::bytes(reinterpret_cast<const char*>(h.bytes), sizeof(h.bytes)));
+}
+
+uintptr_t py_ipc_open(py::bytes handle) {
+  const std::string s = handle;
+  if (s.size() != sizeof(fa_ipc_handle)) throw std::runtime_error("IPC handle must be 64 bytes");
+  fa_ipc_handle h;
+  std::memcpy(h.bytes, s.data(), sizeof(h.bytes));
+  void* p = nullptr;
+  fa_status st = fa_ipc_open(&h, &p);
+  if (st != FA_OK) throw std::runtime_error(err_text(st));
+  return reinterpret_cast<uintptr_t>(p);
+}
+
 // ------------------------------------------------------------ module API
 bool py_initialize() {
   fa_status st = fa_init(g_device);
@@ -383,4 +563,24 @@ PYBIND11_MODULE(_flash_attn_metal, m) {
     fa_status st = fa_pool_clear();
     if (st != FA_OK) throw std::runtime_error(err_text(st));
   });
+  m.def("forward_range", &py_forward_range, py::arg("Q"), py::arg("K"), py::arg("V"), py::arg("q_range"),
+        py::arg("kv_range"), py::arg("out") = py::none(), py::arg("lse") = py::none(), py::kw_only(),
+        py::arg("softmax_scale") = 0.0f, py::arg("is_causal") = false, py::arg("cos") = py::none(),
+        py::arg("sin") = py::none(), py::arg("rope_theta") = py::none(), py::arg("out_dtype") = py::none(),
+        py::arg("route") = py::none(), py::arg("n_owners") = 0, py::arg("owner_rows") = 0,
+        "Rows q_range of the attention over keys kv_range (CUDA tensors, current stream)");
+  m.def("combine", &py_combine, py::arg("o_parts"), py::arg("lse_parts"), py::arg("out"),
+        py::arg("lse") = py::none(), py::arg("q_range") = py::none(),
+        "Merge split-KV partials (O_j, LSE_j) into out (CUDA tensors, current stream)");
+  m.def("ipc_alloc", &py_ipc_alloc, py::arg("bytes"),
+        "Allocate device memory shareable with other processes: (address, 64-byte handle)");
+  m.def("ipc_open", &py_ipc_open, py::arg("handle"), "Map a peer process's allocation; returns its address");
+  m.def("ipc_close", [](uintptr_t p) {
+    fa_status st = fa_ipc_close(reinterpret_cast<void*>(p));
+    if (st != FA_OK) throw std::runtime_error(err_text(st));
+  }, py::arg("address"));
+  m.def("ipc_free", [](uintptr_t p) {
+    fa_status st = fa_ipc_free(reinterpret_cast<void*>(p));
+    if (st != FA_OK) throw std::runtime_error(err_text(st));
+  }, py::arg("address"));
 }

@@ -366,7 +366,7 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
   AttnArgs& a = pl.a;
   a.status = ds->status;
   if (a.q_end <= a.q_begin || a.B == 0 || a.Hq == 0) return FA_OK;
-  if (!a.o) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
+  if (!a.o && a.route_rows == 0) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
   // No key at all (Sk == 0 or an empty split): O = 0, LSE = -inf.
   if (a.kv_end <= a.kv_begin) {
     cudaError_t e = launch_fill_empty(a, pl.out_dtype, stream);
@@ -405,7 +405,7 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
   }
 
   // Tensor-core path.
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(a.o))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (a.route_rows == 0 && !aligned16(a.o)))
     return fail(FA_ERR_INVALID_ARG, "tensor base addresses must be 16-byte aligned");
   if (pl.ws_bytes > 0) {
     if (workspace == nullptr) {
@@ -431,18 +431,28 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
   int64_t v_sb = a.v_sb, v_ss = a.v_ss, v_sh = a.v_sh;
   bool qk_bf16 = (pl.dtype == kBF16);
   cudaError_t e;
+  // Only the rows the kernel's tiles can load are staged: the query range and
+  // the key range, each rounded up to whole 128-row tiles.
+  const size_t esz = dtype_size(pl.dtype);
+  const int q_lo = a.q_begin, q_hi = std::min(a.Sq, a.q_begin + (a.q_end - a.q_begin + 127) / 128 * 128);
+  const int k_lo = a.kv_begin, k_hi = std::min(a.Sk, a.kv_begin + (a.kv_end - a.kv_begin + 127) / 128 * 128);
+  const int hd = a.D / 2;
   if (pl.need_q16) {
     __half* y = take((size_t)a.B * a.Sq * a.Hq * a.D * 2);
-    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y,
-                         ds->status, stream);
+    e = launch_prep_fp16(static_cast<const uint8_t*>(q) + (size_t)q_lo * a.q_ss * esz, pl.dtype, a.q_sb,
+                         a.q_ss, a.q_sh, a.B, q_hi - q_lo, a.Hq, a.D, cs ? cs + (size_t)q_lo * hd : nullptr,
+                         sn ? sn + (size_t)q_lo * hd : nullptr, y + (size_t)q_lo * a.Hq * a.D,
+                         a.Sq, ds->status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep Q");
     qs = y;
     q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
   }
   if (pl.need_k16) {
     __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y,
-                         ds->status, stream);
+    e = launch_prep_fp16(static_cast<const uint8_t*>(k) + (size_t)k_lo * a.k_ss * esz, pl.dtype, a.k_sb,
+                         a.k_ss, a.k_sh, a.B, k_hi - k_lo, a.Hk, a.D, cs ? cs + (size_t)k_lo * hd : nullptr,
+                         sn ? sn + (size_t)k_lo * hd : nullptr, y + (size_t)k_lo * a.Hk * a.D,
+                         a.Sk, ds->status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep K");
     ks = y;
     k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
@@ -450,8 +460,9 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
   if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
   if (pl.need_v16) {
     __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, nullptr, nullptr,
-                         y, ds->status, stream);
+    e = launch_prep_fp16(static_cast<const uint8_t*>(v) + (size_t)k_lo * a.v_ss * esz, pl.dtype, a.v_sb,
+                         a.v_ss, a.v_sh, a.B, k_hi - k_lo, a.Hk, a.D, nullptr, nullptr,
+                         y + (size_t)k_lo * a.Hk * a.D, a.Sk, ds->status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep V");
     vs = y;
     v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
@@ -504,6 +515,7 @@ fa_status fa_init(int device) {
     cudaGetLastError();
     return fail(FA_ERR_NO_DEVICE, "no CUDA device visible");
   }
+  if (device == -1) FA_CUDA(cudaGetDevice(&device));  // the calling thread's current device
   if (device < 0 || device >= n) return fail(FA_ERR_INVALID_ARG, "device index out of range");
   FA_CUDA(cudaSetDevice(device));
   DeviceState* ds = nullptr;
@@ -520,6 +532,7 @@ fa_status fa_device_info(int device, char* name, size_t name_len, uint64_t* tota
     if (initialized) *initialized = 0;
     return fail(FA_ERR_NO_DEVICE, "no CUDA device visible");
   }
+  if (device == -1) FA_CUDA(cudaGetDevice(&device));
   if (device < 0 || device >= n) return fail(FA_ERR_INVALID_ARG, "device index out of range");
   cudaDeviceProp prop;
   FA_CUDA(cudaGetDeviceProperties(&prop, device));
@@ -599,6 +612,84 @@ fa_status fa_combine(const fa_params* p, const float* o_parts, const float* lse_
   pl.a.lse = lse;
   cudaError_t e = launch_combine(pl.a, o_parts, lse_parts, n_splits, pl.out_dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "combine");
+}
+
+fa_status fa_forward_range(const fa_params* p, const void* q, const void* k, const void* v, void* o,
+                           float* lse, const float* cos, const float* sin, uint32_t q_begin,
+                           uint32_t q_end, uint32_t kv_begin, uint32_t kv_end, const fa_route* route,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (!p) return fail(FA_ERR_INVALID_ARG, "params is NULL");
+  fa_params pp = *p;
+  if (route) pp.o_stride[0] = pp.o_stride[1] = pp.o_stride[2] = 0;  // slots are contiguous
+  Plan pl;
+  fa_status st = make_plan(&pp, &pl);
+  if (st != FA_OK) return st;
+  if (q_begin > q_end || q_end > p->seqlen_q || kv_begin > kv_end || kv_end > p->seqlen_k)
+    return fail(FA_ERR_INVALID_ARG, "row ranges out of bounds");
+  AttnArgs& a = pl.a;
+  if (route) {
+    if (!route->table || route->n_owners <= 0 || route->owner_rows == 0 || route->owner_rows % 128 != 0)
+      return fail(FA_ERR_INVALID_ARG, "route needs a table, n_owners > 0 and owner_rows a multiple of 128");
+    if ((uint64_t)route->n_owners * route->owner_rows < q_end)
+      return fail(FA_ERR_INVALID_ARG, "route does not cover the query range");
+    // Every 128-row tile must fall inside one owner's block.
+    if (q_begin % 128 != 0) return fail(FA_ERR_INVALID_ARG, "routed q_begin must be a multiple of 128");
+    a.route = reinterpret_cast<const unsigned long long*>(route->table);
+    a.route_n = route->n_owners;
+    a.route_rows = (int)route->owner_rows;
+    o = nullptr;  // rows go to the owners' slots
+    lse = nullptr;
+  }
+  DeviceState* ds = nullptr;
+  st = device_state(&ds);
+  if (st != FA_OK) return st;
+  a.q_begin = (int)q_begin;
+  a.q_end = (int)q_end;
+  a.kv_begin = (int)kv_begin;
+  a.kv_end = (int)kv_end;
+  a.o = o;
+  a.lse = lse;
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+}
+
+// ------------------------------------------------------------ CUDA IPC
+// Staging buffers that peers write split-KV partials into. Plain cudaMalloc
+// memory (the only kind cudaIpcGetMemHandle accepts), opened by peers with
+// lazy peer access; plain device memory, nothing else is mapped.
+static_assert(sizeof(fa_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+
+fa_status fa_ipc_alloc(size_t bytes, void** dev_ptr, fa_ipc_handle* handle) {
+  if (!dev_ptr || !handle || bytes == 0) return fail(FA_ERR_INVALID_ARG, "bad fa_ipc_alloc arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (IPC staging)");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "cudaIpcGetMemHandle");
+  }
+  std::memcpy(handle->bytes, &h, sizeof(h));
+  *dev_ptr = p;
+  return FA_OK;
+}
+
+fa_status fa_ipc_free(void* dev_ptr) {
+  cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "cudaFree (IPC staging)");
+}
+
+fa_status fa_ipc_open(const fa_ipc_handle* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return fail(FA_ERR_INVALID_ARG, "bad fa_ipc_open arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle->bytes, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+fa_status fa_ipc_close(void* dev_ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? FA_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
 }
 
 fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, const void* v, void* o,
@@ -968,7 +1059,7 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
   if (pl.need_q16) {
     __half* y = reinterpret_cast<__half*>(wp);
     wp += up256((size_t)a.B * a.Sq * a.Hq * a.D * 2);
-    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y, nd.status, stream);
+    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y, a.Sq, nd.status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep Q");
     qs = y;
     q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
@@ -976,7 +1067,7 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
   if (pl.need_k16) {
     __half* y = reinterpret_cast<__half*>(wp);
     wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y, nd.status, stream);
+    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y, a.Sk, nd.status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep K");
     ks = y;
     k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
@@ -986,7 +1077,7 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
     __half* y = reinterpret_cast<__half*>(wp);
     wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
     e = launch_prep_fp16(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, nullptr, nullptr, y,
-                         nd.status, stream);
+                         a.Sk, nd.status, stream);
     if (e != cudaSuccess) return cuda_fail(e, "prep V");
     vs = y;
     v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;

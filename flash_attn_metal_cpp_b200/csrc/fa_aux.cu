@@ -70,7 +70,7 @@ __device__ __forceinline__ bool store8_half(__half* p, const float (&x)[8]) {
 template <typename T, bool ROPE>
 __global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss, int64_t sh, int S,
                                  int H, int D, long long n_rows, const float* __restrict__ cs,
-                                 const float* __restrict__ sn, __half* __restrict__ y,
+                                 const float* __restrict__ sn, __half* __restrict__ y, int y_rows,
                                  unsigned* status) {
   const int chunks = ROPE ? D / 16 : D / 8;
   const long long total = n_rows * chunks;
@@ -84,7 +84,7 @@ __global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss
     const int s = (int)(bs % S);
     const int b = (int)(bs / S);
     const T* src = x + (int64_t)b * sb + (int64_t)s * ss + (int64_t)h * sh;
-    __half* dst = y + rowi * D;
+    __half* dst = y + (((int64_t)b * y_rows + s) * H + h) * D;  // y: [B, y_rows, H, D]
     if (ROPE) {
       const int half = D / 2;
       const int c0 = ch * 8;
@@ -115,7 +115,8 @@ __global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss
 
 template <typename T>
 cudaError_t prep_t(const void* x, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H, int D,
-                   const float* cs, const float* sn, __half* y, unsigned* status, cudaStream_t st) {
+                   const float* cs, const float* sn, __half* y, int y_rows, unsigned* status,
+                   cudaStream_t st) {
   const long long n_rows = (long long)B * S * H;
   const long long total = n_rows * (cs ? D / 16 : D / 8);
   if (total == 0) return cudaSuccess;
@@ -124,10 +125,10 @@ cudaError_t prep_t(const void* x, int64_t sb, int64_t ss, int64_t sh, int B, int
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (cs)
     prep_fp16_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(
-        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, status);
+        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, y_rows, status);
   else
     prep_fp16_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(
-        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, status);
+        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, y_rows, status);
   note_launch();
   return cudaGetLastError();
 }
@@ -174,23 +175,40 @@ __global__ void combine_kernel(const AttnArgs a, const float* __restrict__ o_par
   const long long o_stride = (long long)a.B * a.Sq * a.Hq * a.D;
   const long long lse_idx = ((long long)b * a.Hq + h) * a.Sq + q;
   const long long o_row = (((long long)b * a.Sq + q) * a.Hq + h) * a.D;
+  // Lane j (< 32) holds LSE_j; larger split counts fold in 32 at a time.
   float mx = -INFINITY;
-  for (int j = 0; j < n_splits; ++j) mx = fmaxf(mx, lse_parts[j * lse_stride + lse_idx]);
+  for (int j = lane; j < n_splits; j += 32) mx = fmaxf(mx, lse_parts[j * lse_stride + lse_idx]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   float w_sum = 0.f;
-  for (int j = 0; j < n_splits; ++j) {
+  for (int j = lane; j < n_splits; j += 32) {
     const float l = lse_parts[j * lse_stride + lse_idx];
     w_sum += (l == -INFINITY) ? 0.f : expf(l - mx);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) w_sum += __shfl_xor_sync(0xffffffffu, w_sum, off);
   const float lse = (w_sum > 0.f) ? mx + logf(w_sum) : -INFINITY;
   OutT* orow = reinterpret_cast<OutT*>(a.o) + (int64_t)b * a.o_sb + (int64_t)q * a.o_ss +
                (int64_t)h * a.o_sh;
-  for (int d = lane; d < a.D; d += 32) {
-    float acc = 0.f;
-    for (int j = 0; j < n_splits; ++j) {
-      const float l = lse_parts[j * lse_stride + lse_idx];
-      if (l != -INFINITY) acc += expf(l - lse) * o_parts[j * o_stride + o_row + d];
+  // Each lane owns columns lane, lane+32, ... (head_dim <= 256: at most 8).
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j = 0; j < n_splits; ++j) {
+    const float l = lse_parts[j * lse_stride + lse_idx];
+    if (l == -INFINITY) continue;  // split saw no key of this row
+    const float w = expf(l - lse);
+    const float* src = o_parts + j * o_stride + o_row;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < a.D) acc[i] = fmaf(w, src[d], acc[i]);
     }
-    orow[d] = cvt_out<OutT>(acc);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < a.D) orow[d] = cvt_out<OutT>(acc[i]);
   }
   if (lane == 0 && a.lse != nullptr) a.lse[lse_idx] = lse;
 }
@@ -207,10 +225,11 @@ __global__ void fill_empty_kernel(const AttnArgs a) {
     const long long bq = r / a.Hq;
     const int q = a.q_begin + (int)(bq % nq);
     const int b = (int)(bq / nq);
-    OutT* orow = reinterpret_cast<OutT*>(a.o) + (int64_t)b * a.o_sb + (int64_t)q * a.o_ss +
-                 (int64_t)h * a.o_sh;
+    const RowDst dst = row_dst(a, q);
+    OutT* orow = reinterpret_cast<OutT*>(dst.o) + (int64_t)b * dst.o_sb + (int64_t)dst.row * dst.o_ss +
+                 (int64_t)h * dst.o_sh;
     orow[d] = cvt_out<OutT>(0.f);
-    if (d == 0 && a.lse != nullptr) a.lse[((long long)b * a.Hq + h) * a.Sq + q] = -INFINITY;
+    if (d == 0 && dst.lse != nullptr) dst.lse[((long long)b * a.Hq + h) * dst.lse_rows + dst.row] = -INFINITY;
   }
 }
 
@@ -218,11 +237,11 @@ __global__ void fill_empty_kernel(const AttnArgs a) {
 
 cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B,
                              int S, int H, int D, const float* cs, const float* sn, __half* y,
-                             unsigned* status, cudaStream_t st) {
+                             int y_rows, unsigned* status, cudaStream_t st) {
   switch (in_dtype) {
-    case kF16: return prep_t<__half>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
-    case kBF16: return prep_t<__nv_bfloat16>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
-    default: return prep_t<float>(x, sb, ss, sh, B, S, H, D, cs, sn, y, status, st);
+    case kF16: return prep_t<__half>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
+    case kBF16: return prep_t<__nv_bfloat16>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
+    default: return prep_t<float>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
   }
 }
 

@@ -155,14 +155,16 @@ __global__ void __launch_bounds__(THREADS)
 
   if (!row_ok) return;
   const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
-  const int64_t orow = (int64_t)bz * a.o_sb + (int64_t)row_g * a.o_ss + (int64_t)hq * a.o_sh;
+  const RowDst dst = row_dst(a, row_g);
+  const int64_t orow = (int64_t)bz * dst.o_sb + (int64_t)dst.row * dst.o_ss + (int64_t)hq * dst.o_sh;
 #pragma unroll
   for (int i = 0; i < DPT; ++i) {
     const int col = i * TPR + c;
-    if (col < D) store_out(a.o, orow + col, out_dtype, o[i] * inv_l);
+    if (col < D) store_out(dst.o, orow + col, out_dtype, o[i] * inv_l);
   }
-  if (c == 0 && a.lse != nullptr)
-    a.lse[((int64_t)bz * a.Hq + hq) * a.Sq + row_g] = (l_run > 0.f) ? m_run + logf(l_run) : -INFINITY;
+  if (c == 0 && dst.lse != nullptr)
+    dst.lse[((int64_t)bz * a.Hq + hq) * dst.lse_rows + dst.row] =
+        (l_run > 0.f) ? m_run + logf(l_run) : -INFINITY;
 }
 
 template <typename InT, int DMAX>

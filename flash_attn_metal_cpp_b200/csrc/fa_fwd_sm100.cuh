@@ -422,12 +422,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && q0 + t * BM < a.q_end) {
       const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
-      if (row_ok && a.lse != nullptr) {
+      // Routed slots are a multiple of BM rows, so the tile's first row
+      // names the owner of all its rows.
+      RowDst dst = row_dst(a, q0 + t * BM);
+      dst.row += row;
+      if (row_ok && dst.lse != nullptr) {
         const float lse = (l_run > 0.f) ? (m_run + log2f(l_run)) * 0.69314718055994531f : -INFINITY;
-        a.lse[((int64_t)bz * a.Hq + hq) * a.Sq + row_g] = lse;
+        dst.lse[((int64_t)bz * a.Hq + hq) * dst.lse_rows + dst.row] = lse;
       }
-      OutT* orow = reinterpret_cast<OutT*>(a.o) + (int64_t)bz * a.o_sb + (int64_t)row_g * a.o_ss +
-                   (int64_t)hq * a.o_sh;
+      OutT* orow = reinterpret_cast<OutT*>(dst.o) + (int64_t)bz * dst.o_sb + (int64_t)dst.row * dst.o_ss +
+                   (int64_t)hq * dst.o_sh;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float v[32];

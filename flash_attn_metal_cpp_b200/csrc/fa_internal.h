@@ -32,7 +32,42 @@ struct AttnArgs {
   const float* rope_cos;   // [rows, D/2] (SIMT kernel applies RoPE on load when non-NULL)
   const float* rope_sin;
   unsigned* status;        // device status word (timeouts, range errors)
+  // Routed output (split-KV across devices): when route_rows > 0, query row r
+  // is owned by owner r / route_rows and its O / LSE go to that owner's
+  // staging slot instead of o / lse: route[owner] is the slot's O base
+  // (contiguous [B, route_rows, Hq, D]), route[route_n + owner] its LSE base
+  // ([B, Hq, route_rows]). Slots may live in peer-device memory.
+  const unsigned long long* route;
+  int route_n;
+  int route_rows;
 };
+
+// Where the O row / LSE entry of absolute query row `row` go.
+struct RowDst {
+  void* o;
+  float* lse;
+  int row;                 // row index inside that destination
+  int lse_rows;            // LSE row stride of that destination
+  int64_t o_sb, o_ss, o_sh;
+};
+
+#ifdef __CUDACC__
+__device__ __forceinline__ RowDst row_dst(const AttnArgs& a, int row) {
+  if (a.route_rows > 0) {
+    const int owner = row / a.route_rows;
+    RowDst d;
+    d.o = reinterpret_cast<void*>(a.route[owner]);
+    d.lse = reinterpret_cast<float*>(a.route[a.route_n + owner]);
+    d.row = row - owner * a.route_rows;
+    d.lse_rows = a.route_rows;
+    d.o_ss = (int64_t)a.Hq * a.D;
+    d.o_sh = a.D;
+    d.o_sb = (int64_t)a.route_rows * d.o_ss;
+    return d;
+  }
+  return RowDst{a.o, a.lse, row, a.Sq, a.o_sb, a.o_ss, a.o_sh};
+}
+#endif
 
 // Element type codes shared with fa_b200.h.
 enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
@@ -46,11 +81,13 @@ cudaError_t launch_attn_sm100(const AttnArgs& a, const CUtensorMap& tq, const CU
 // Generic CUDA-core path: any head_dim <= 256, fp32/fp16/bf16 inputs.
 cudaError_t launch_attn_simt(const AttnArgs& a, int in_dtype, int out_dtype, cudaStream_t stream);
 
-// RoPE / format pre-pass: y = rope(x) (if cos != NULL) converted to fp16,
-// written contiguous BSHD. x has strides (sb, ss, sh).
+// RoPE / format pre-pass over S rows: y = rope(x) (if cos != NULL) converted
+// to fp16. x has strides (sb, ss, sh); y is contiguous [B, y_rows, H, D]
+// (y_rows >= S, so a row range of a larger tensor can be staged in place).
+// Row s uses table row s of cos/sin.
 cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh,
                              int B, int S, int H, int D, const float* cos, const float* sin,
-                             __half* y, unsigned* status, cudaStream_t stream);
+                             __half* y, int y_rows, unsigned* status, cudaStream_t stream);
 
 // cos/sin tables [rows, D/2] in float32 from theta, computed in double.
 cudaError_t launch_rope_table(float* cos, float* sin, int rows, int D, double theta,

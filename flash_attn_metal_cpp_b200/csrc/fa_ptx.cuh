@@ -99,7 +99,7 @@ __device__ __forceinline__ bool fa_wait(uint32_t bar, uint32_t parity, unsigned*
 
 // ---------------------------------------------------------------- TMA
 // 4-D tiled bulk tensor load global -> shared, completion counted in bytes
-// on `bar`. No multicast: each CTA loads its own tiles.
+// on `bar`. Each CTA loads its own tiles (no cluster sharing).
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint32_t bar, int c0,
                                             int c1, int c2, int c3) {
   asm volatile(

@@ -25,7 +25,10 @@
  *   fa_forward_partial   <- (no counterpart) split-KV partial used by the multi-GPU
  *                           long-context path; same kernel as fa_forward
  *   fa_combine           <- (no counterpart) (O, LSE) merge of split-KV partials
- *   fa_last_error        <- std::cerr messages / RuntimeError text
+ *   fa_forward_range     <- (no counterpart) row/key-range forward with optional
+ *                           output routing to peer devices (split-KV over NVLink)
+ *   fa_ipc_*             <- (no counterpart) CUDA IPC staging buffers for the routing
+ *   fa_last_error       <- std::cerr messages / RuntimeError text
  *                                                            python/bindings.cpp:46-49,224-232
  *
  * Layout contract (same as the reference API, python/bindings.cpp:142-159):
@@ -101,11 +104,13 @@ typedef struct fa_params {
 /* Fill `p` with the reference defaults (scale 0, no mask, no RoPE, contiguous). */
 void fa_params_init(fa_params* p);
 
-/* Select and initialise CUDA device `device` for the calling thread. */
+/* Select and initialise CUDA device `device` for the calling thread
+ * (-1: the thread's current device, left selected). */
 fa_status fa_init(int device);
 
 /* Device name (NUL-terminated, truncated to name_len), total global memory
- * in bytes, and whether fa_init succeeded on it. Any output may be NULL. */
+ * in bytes, and whether fa_init succeeded on it (-1: the current device).
+ * Any output may be NULL. */
 fa_status fa_device_info(int device, char* name, size_t name_len,
                          uint64_t* total_mem, int* initialized);
 
@@ -159,6 +164,50 @@ fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k,
 fa_status fa_combine(const fa_params* p, const float* o_parts,
                      const float* lse_parts, int32_t n_splits, void* o,
                      float* lse, uint32_t q_begin, uint32_t q_end, void* stream);
+
+/* Output routing for a split-KV partial spread over devices. Query rows are
+ * owned in blocks of owner_rows (a multiple of 128): row r belongs to owner
+ * r / owner_rows. `table` is a DEVICE array of 2 * n_owners addresses:
+ *   table[o]            O slot of owner o: [batch, owner_rows, Hq, D] of
+ *                       p->out_dtype, contiguous, 16-byte aligned
+ *   table[n_owners + o] LSE slot of owner o: [batch, Hq, owner_rows] float32
+ * Slots may be peer-device memory (fa_ipc_open): the kernel's epilogue then
+ * stores each finished tile straight over NVLink. */
+typedef struct fa_route {
+  const uint64_t* table;
+  int32_t n_owners;
+  uint32_t owner_rows;
+} fa_route;
+
+/* Rows [q_begin, q_end) of softmax(scale Q K^T + mask) V restricted to keys
+ * [kv_begin, kv_end) (no counterpart in the reference; the building block of
+ * the multi-GPU paths). Output dtype p->out_dtype; rows are written to o /
+ * lse (lse may be NULL) or, when route != NULL, to the owners' slots (o and
+ * lse are ignored; q_begin must then be a multiple of 128 and
+ * n_owners * owner_rows >= q_end). Rows that see no key of the range get O = 0 and
+ * LSE = -inf. Query and key positions are absolute (RoPE tables and the
+ * causal mask use them). */
+fa_status fa_forward_range(const fa_params* p, const void* q, const void* k,
+                           const void* v, void* o, float* lse,
+                           const float* cos, const float* sin,
+                           uint32_t q_begin, uint32_t q_end,
+                           uint32_t kv_begin, uint32_t kv_end,
+                           const fa_route* route, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* Device memory shared between the processes of one node (CUDA IPC; no
+ * counterpart in the reference). fa_ipc_alloc allocates on the current
+ * device and returns a handle another process passes to fa_ipc_open to map
+ * the same memory (peer access over NVLink). fa_ipc_close unmaps an opened
+ * handle; fa_ipc_free releases an allocation (after every peer closed it). */
+typedef struct fa_ipc_handle {
+  unsigned char bytes[64];
+} fa_ipc_handle;
+
+fa_status fa_ipc_alloc(size_t bytes, void** dev_ptr, fa_ipc_handle* handle);
+fa_status fa_ipc_free(void* dev_ptr);
+fa_status fa_ipc_open(const fa_ipc_handle* handle, void** dev_ptr);
+fa_status fa_ipc_close(void* dev_ptr);
 
 /* Build float32 cos/sin tables [rows, head_dim/2] on the host:
  * angle(pos, i) = pos * theta^(-2i/head_dim). */

@@ -176,6 +176,6 @@ def combine_partials(o_parts, lse_parts):
 
 
 def attention_flops(B: int, Sq: int, Sk: int, Hq: int, D: int, causal: bool) -> float:
-    """Headline FLOP count 4*B*H*Sq*Sk*D, halved for causal (BASELINE convention)."""
+    """Headline FLOP count 4*B*H*Sq*Sk*D, halved for causal (softmax and RoPE not counted)."""
     f = 4.0 * B * Hq * Sq * Sk * D
     return f / 2 if causal else f

@@ -51,19 +51,31 @@ def _worker(rank, world, port, mode, result_path):
         t = torch.from_numpy(out)
         dist.all_reduce(t)  # disjoint shards: the sum assembles the full output
         result = t.numpy()
-    else:  # split-KV: partial (O, LSE) per rank over its zig-zag key chunks, then combine
-        parts_o, parts_l = [], []
-        for kv in sharding.splitkv_chunks(S, world, align=16)[rank]:
-            o, l = orc.attention_ref(q, k, v, causal=True, softmax_scale=0.25, return_lse=True, kv_range=kv)
-            parts_o.append(o)
-            parts_l.append(l)
-        o_all = [torch.zeros(2, *q.shape) for _ in range(world)]
-        l_all = [torch.zeros(2, B, Hq, S) for _ in range(world)]
-        dist.all_gather(o_all, torch.from_numpy(np.stack(parts_o)))
-        dist.all_gather(l_all, torch.from_numpy(np.stack(parts_l)))
-        o_cat = torch.cat(o_all).numpy()
-        l_cat = torch.cat(l_all).numpy()
-        result, _ = orc.combine_partials(o_cat, l_cat)
+    else:  # split-KV: balanced key range per rank, partials routed to row owners' slots, owners merge
+        plan = sharding.splitkv_plan(S, S, world, causal=True, tile=16)
+        klo, khi = plan.kv_ranges[rank]
+        qlo, qhi = plan.q_ranges[rank]
+        part_o = np.zeros_like(q)
+        part_l = np.full((B, Hq, S), -np.inf, np.float32)
+        if qhi > qlo:
+            part_o, part_l = orc.attention_ref(q, k, v, causal=True, softmax_scale=0.25, return_lse=True,
+                                               kv_range=(klo, khi), q_range=(qlo, qhi))
+        # The kernel epilogue stores rows into peers' slots; here the slots are
+        # filled from an all_gather of every rank's partial, following the plan.
+        o_all = [torch.zeros(*q.shape) for _ in range(world)]
+        l_all = [torch.zeros(B, Hq, S) for _ in range(world)]
+        dist.all_gather(o_all, torch.from_numpy(np.ascontiguousarray(part_o, dtype=np.float32)))
+        dist.all_gather(l_all, torch.from_numpy(np.ascontiguousarray(part_l, dtype=np.float32)))
+        block = np.zeros_like(q)
+        lo, hi = plan.owner_block(rank)
+        if hi > lo:
+            slots = plan.slots[rank]
+            st_o = np.stack([o_all[r].numpy()[:, lo:hi] for r in slots])
+            st_l = np.stack([l_all[r].numpy()[:, :, lo:hi] for r in slots])
+            block[:, lo:hi], _ = orc.combine_partials(st_o, st_l)
+        t = torch.from_numpy(block)
+        dist.all_reduce(t)  # owner blocks are disjoint
+        result = t.numpy()
     if rank == 0:
         np.save(result_path, result)
     dist.barrier()
@@ -101,3 +113,37 @@ def test_zigzag_chunks_balance_causal_work():
         assert all(a[1] == b[0] for a, b in zip(flat, flat[1:]))
         work = [sum(sharding.causal_work(S, c) for c in r) for r in chunks]
         assert max(work) / min(work) < 1.01
+
+
+@pytest.mark.parametrize("Sq,Sk,W,causal", [(65536, 65536, 2, True), (65536, 65536, 8, True), (4096, 4096, 4, True),
+                                            (1000, 300, 3, True), (300, 1000, 4, False), (200, 200, 8, True)])
+def test_splitkv_plan_covers_and_balances(Sq, Sk, W, causal):
+    p = sharding.splitkv_plan(Sq, Sk, W, causal)
+    # Key ranges tile [0, Sk) in order.
+    assert p.kv_ranges[0][0] == 0 and p.kv_ranges[-1][1] == Sk
+    assert all(a[1] == b[0] for a, b in zip(p.kv_ranges, p.kv_ranges[1:]))
+    assert all(lo % p.tile == 0 or lo == Sk for lo, _ in p.kv_ranges)
+    # Owner blocks tile [0, Sq) with tile-multiple sizes.
+    assert p.owner_rows % p.tile == 0 and p.n_owners <= W
+    assert p.owner_block(p.n_owners - 1)[1] == Sq
+    for r, ((klo, khi), (qlo, qhi)) in enumerate(zip(p.kv_ranges, p.q_ranges)):
+        if khi <= klo:
+            assert qhi == qlo
+            continue
+        # Every row that sees a key of the range is computed, starting on an owner boundary.
+        first_row = klo if causal else 0
+        if first_row < Sq:
+            assert qlo <= first_row and qhi == Sq and qlo % p.owner_rows == 0
+    # Slots: owner o merges exactly the ranks whose query range covers its block.
+    for o in range(p.n_owners):
+        lo, hi = p.owner_block(o)
+        want = [r for r in range(W) if p.q_ranges[r][0] <= lo and p.q_ranges[r][1] >= hi and p.q_ranges[r][1] > p.q_ranges[r][0]]
+        assert p.slots[o] == want and len(want) >= 1
+    # Balance: no share exceeds the even share by more than one key tile's work
+    # (the granularity of a contiguous tile-aligned cut); long sequences within 5%.
+    work = [p.pair_work(r) for r in range(W)]
+    tile_max = max(sharding.causal_work(Sq, (t, min(Sk, t + p.tile))) if causal else min(p.tile, Sk - t) * Sq
+                   for t in range(0, Sk, p.tile))
+    assert max(work) <= sum(work) / W + tile_max
+    if Sq >= 65536:
+        assert max(work) / min(work) < 1.05
