@@ -727,20 +727,33 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
   const float* tc = tables ? static_cast<const float*>(dc.p) : nullptr;
   const float* tsn = tables ? static_cast<const float*>(dsn.p) : nullptr;
 
-  // Independent chunks: whole batches, or (batch 1) groups of KV heads with
-  // their query heads. Chunk c's copy in, compute and copy out run on three
-  // streams ordered by events, so transfers overlap the attention kernels.
-  struct Chunk { int b0, nb, hk0, nhk; };
+  // Pipeline over query-row blocks: for each batch, K and V are copied in
+  // first, then Q in blocks of rows, the block with the LAST rows first (under
+  // the causal mask it is the heaviest, and the final block -- whose compute
+  // and copy-out form the tail after the last input byte -- is the lightest).
+  // A block is computed as soon as it has landed, against the keys its rows
+  // can see, and its O rows (contiguous in BSHD) are copied out while later
+  // blocks stream in. Copy in, compute and copy out run on three streams
+  // ordered by events.
+  struct Chunk { int b, r0, r1; bool kv_first; };
   std::vector<Chunk> chunks;
-  const int kMaxChunks = 8;
   const bool small = q_bytes + 2 * k_bytes < (size_t(16) << 20);
-  if (!small && a.B >= 2) {
-    const int per = (a.B + kMaxChunks - 1) / kMaxChunks;
-    for (int b0 = 0; b0 < a.B; b0 += per) chunks.push_back({b0, std::min(per, a.B - b0), 0, a.Hk});
-  } else if (!small && a.B == 1 && a.Hk >= 2) {
-    const int n = std::min(a.Hk, kMaxChunks);
-    const int per = (a.Hk + n - 1) / n;
-    for (int h0 = 0; h0 < a.Hk; h0 += per) chunks.push_back({0, 1, h0, std::min(per, a.Hk - h0)});
+  if (!small && a.Sq > 0) {
+    // About 16 blocks in all, each still filling the GPU (>= 2 CTAs of 256
+    // rows per SM). (Measured on cfg4: finer blocks lengthen the input
+    // stream -- smaller copies and more copy-out interleaving -- and make the
+    // kernels of the last batch trail the copies; 12 blocks end 0.8 ms after
+    // the last input byte and are the fastest of the splits tried.)
+    const long long max_blocks = std::max<long long>(1, (long long)a.Sq * a.Hq / (256LL * 296));
+    const int per_batch = (int)std::min<long long>(std::max(1, (16 + a.B - 1) / a.B), max_blocks);
+    // Block starts are multiples of 256 rows, so every CTA (and every warp's
+    // rows) is the same as in a one-piece launch and the results are
+    // bit-identical to fa_forward's.
+    const int rows = ((a.Sq + per_batch - 1) / per_batch + 255) / 256 * 256;
+    const int n_blk = (a.Sq + rows - 1) / rows;
+    for (int b = 0; b < a.B; ++b)
+      for (int i = n_blk - 1; i >= 0; --i)
+        chunks.push_back({b, i * rows, std::min(a.Sq, (i + 1) * rows), i == n_blk - 1});
   }
   if (chunks.size() <= 1 || q_bytes == 0 || k_bytes == 0) {
     // One piece: copy in, run, copy out on one stream.
@@ -786,66 +799,53 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
       cudaEventDestroy(ev_done[c]);
     }
   };
-  // Copy `rows` rows of `width` bytes between tensors with `pitch`-byte rows.
-  auto copy_rows = [](void* dst, const void* src, size_t width, size_t pitch, size_t rows, cudaMemcpyKind kind,
-                      cudaStream_t st) -> cudaError_t {
-    if (width == pitch) return cudaMemcpyAsync(dst, src, width * rows, kind, st);
-    return cudaMemcpy2DAsync(dst, pitch, src, pitch, width, rows, kind, st);
-  };
-  const int group = a.group;
+  const size_t q_row = (size_t)a.Hq * a.D, k_row = (size_t)a.Hk * a.D;  // elements per sequence row
   st = FA_OK;
   for (size_t c = 0; c < chunks.size() && st == FA_OK; ++c) {
     const Chunk& ch = chunks[c];
-    const int hq0 = ch.hk0 * group, nhq = ch.nhk * group;
-    const size_t q_off = ((size_t)ch.b0 * a.Sq * a.Hq + hq0) * a.D;   // elements
-    const size_t k_off = ((size_t)ch.b0 * a.Sk * a.Hk + ch.hk0) * a.D;
-    const size_t q_rows = (size_t)ch.nb * a.Sq, k_rows = (size_t)ch.nb * a.Sk;
-    const size_t q_pitch = (size_t)a.Hq * a.D, k_pitch = (size_t)a.Hk * a.D;
-    const bool full_heads = (ch.nhk == a.Hk);
-    // copy in
-    cudaError_t e = copy_rows(static_cast<char*>(dq.p) + q_off * in_sz, static_cast<const char*>(q) + q_off * in_sz,
-                              (full_heads ? q_pitch * a.Sq * ch.nb : (size_t)nhq * a.D) * in_sz,
-                              (full_heads ? q_pitch * a.Sq * ch.nb : q_pitch) * in_sz, full_heads ? 1 : q_rows,
-                              cudaMemcpyHostToDevice, s_in);
-    for (int m = 0; m < 2 && e == cudaSuccess; ++m)
-      e = copy_rows(static_cast<char*>(m ? dv.p : dk.p) + k_off * in_sz,
-                    static_cast<const char*>(m ? v : k) + k_off * in_sz,
-                    (full_heads ? k_pitch * a.Sk * ch.nb : (size_t)ch.nhk * a.D) * in_sz,
-                    (full_heads ? k_pitch * a.Sk * ch.nb : k_pitch) * in_sz, full_heads ? 1 : k_rows,
-                    cudaMemcpyHostToDevice, s_in);
+    const size_t k_off = (size_t)ch.b * a.Sk * k_row;                  // elements
+    const size_t q_off = ((size_t)ch.b * a.Sq + ch.r0) * q_row;
+    const size_t nrows = (size_t)(ch.r1 - ch.r0);
+    // copy in: the batch's K and V with its first block, then the block's Q rows
+    cudaError_t e = cudaSuccess;
+    if (ch.kv_first)
+      for (int m = 0; m < 2 && e == cudaSuccess; ++m)
+        e = cudaMemcpyAsync(static_cast<char*>(m ? dv.p : dk.p) + k_off * in_sz,
+                            static_cast<const char*>(m ? v : k) + k_off * in_sz, (size_t)a.Sk * k_row * in_sz,
+                            cudaMemcpyHostToDevice, s_in);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(static_cast<char*>(dq.p) + q_off * in_sz, static_cast<const char*>(q) + q_off * in_sz,
+                          nrows * q_row * in_sz, cudaMemcpyHostToDevice, s_in);
     if (e == cudaSuccess) e = cudaEventRecord(ev_in[c], s_in);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev_in[c], 0);
     if (e != cudaSuccess) {
       st = cuda_fail(e, "chunk copy in");
       break;
     }
-    // compute: the chunk as its own problem over strided views of the full buffers
+    // compute: rows [r0, r1) of batch b against the keys they can see
     Plan sub = pl;
-    sub.a.B = ch.nb;
-    sub.a.Hq = nhq;
-    sub.a.Hk = ch.nhk;
-    sub.ws_bytes = 0;
-    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-    if (sub.need_q16) sub.ws_bytes += up((size_t)ch.nb * a.Sq * nhq * a.D * 2);
-    if (sub.need_k16) sub.ws_bytes += up((size_t)ch.nb * a.Sk * ch.nhk * a.D * 2);
-    if (sub.need_v16) sub.ws_bytes += up((size_t)ch.nb * a.Sk * ch.nhk * a.D * 2);
-    sub.a.o = static_cast<char*>(dout.p) + q_off * out_sz;
-    sub.a.lse = dl.p ? static_cast<float*>(dl.p) + ((size_t)ch.b0 * a.Hq + hq0) * a.Sq : nullptr;
-    st = run(sub, static_cast<const char*>(dq.p) + q_off * in_sz, static_cast<const char*>(dk.p) + k_off * in_sz,
-             static_cast<const char*>(dv.p) + k_off * in_sz, tc, tsn, dws.p, pl.ws_bytes, s, ds);
+    sub.a.B = 1;
+    sub.a.q_begin = ch.r0;
+    sub.a.q_end = ch.r1;
+    sub.a.kv_begin = 0;
+    sub.a.kv_end = a.causal ? std::min(a.Sk, ch.r1) : a.Sk;
+    sub.a.o = static_cast<char*>(dout.p) + (size_t)ch.b * a.Sq * q_row * out_sz;
+    sub.a.lse = dl.p ? static_cast<float*>(dl.p) + (size_t)ch.b * a.Hq * a.Sq : nullptr;
+    st = run(sub, static_cast<const char*>(dq.p) + (size_t)ch.b * a.Sq * q_row * in_sz,
+             static_cast<const char*>(dk.p) + k_off * in_sz, static_cast<const char*>(dv.p) + k_off * in_sz, tc, tsn,
+             dws.p, pl.ws_bytes, s, ds);
     if (st != FA_OK) break;
     e = cudaEventRecord(ev_done[c], s);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev_done[c], 0);
-    // copy out
+    // copy out: the block's O rows, and its LSE columns [r0, r1) of every head
     if (e == cudaSuccess)
-      e = copy_rows(static_cast<char*>(o) + q_off * out_sz, static_cast<const char*>(dout.p) + q_off * out_sz,
-                    (full_heads ? q_pitch * a.Sq * ch.nb : (size_t)nhq * a.D) * out_sz,
-                    (full_heads ? q_pitch * a.Sq * ch.nb : q_pitch) * out_sz, full_heads ? 1 : q_rows,
-                    cudaMemcpyDeviceToHost, s_out);
+      e = cudaMemcpyAsync(static_cast<char*>(o) + q_off * out_sz, static_cast<const char*>(dout.p) + q_off * out_sz,
+                          nrows * q_row * out_sz, cudaMemcpyDeviceToHost, s_out);
     if (e == cudaSuccess && lse) {
-      const size_t l_off = ((size_t)ch.b0 * a.Hq + hq0) * a.Sq;
-      e = cudaMemcpyAsync(lse + l_off, static_cast<const float*>(dl.p) + l_off,
-                          (size_t)ch.nb * nhq * a.Sq * sizeof(float), cudaMemcpyDeviceToHost, s_out);
+      const size_t l_off = (size_t)ch.b * a.Hq * a.Sq + ch.r0;
+      e = cudaMemcpy2DAsync(lse + l_off, (size_t)a.Sq * sizeof(float), static_cast<const float*>(dl.p) + l_off,
+                            (size_t)a.Sq * sizeof(float), nrows * sizeof(float), (size_t)a.Hq,
+                            cudaMemcpyDeviceToHost, s_out);
     }
     if (e != cudaSuccess) st = cuda_fail(e, "chunk copy out");
   }

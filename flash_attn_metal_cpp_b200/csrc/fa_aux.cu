@@ -97,11 +97,7 @@ __global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss
       const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
       const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
       float ra[8], rb[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        ra[i] = a[i] * cv[i] - bb[i] * sv[i];
-        rb[i] = a[i] * sv[i] + bb[i] * cv[i];
-      }
+      rope_rotate8(a, bb, cv, sv, ra, rb);
       ok &= store8_half(dst + c0, ra);
       ok &= store8_half(dst + c0 + half, rb);
     } else {

@@ -432,19 +432,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       OutT* orow = reinterpret_cast<OutT*>(dst.o) + (int64_t)bz * dst.o_sb + (int64_t)dst.row * dst.o_ss +
                    (int64_t)hq * dst.o_sh;
+      // The whole O row in one go: all TMEM loads in flight, one wait.
+      float ov[D];
+      if (my_kv > 0) {
+        if constexpr (D == 128) tmem_ld128(tO, ov);
+        else tmem_ld64(tO, ov);
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float v[32];
-        if (my_kv > 0) {
-          uint32_t r[32];
-          tmem_ld32(tO + c * 32, r);
+        for (int i = 0; i < D; ++i) ov[i] *= inv_l;
+      } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * inv_l;
-        } else {
+        for (int i = 0; i < D; ++i) ov[i] = 0.f;
+      }
+      if (row_ok) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
-        if (row_ok) store_row32<OutT>(orow + c * 32, v);
+        for (int c = 0; c < D / 32; ++c) store_row32<OutT>(orow + c * 32, ov + c * 32);
       }
     }
   }

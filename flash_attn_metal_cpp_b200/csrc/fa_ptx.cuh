@@ -405,4 +405,17 @@ __device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Rotate-half RoPE of 8 column pairs (x_i, x_{i+D/2}) (common.metal:150-167):
+//   x_i' = x_i cos - x_{i+D/2} sin,  x_{i+D/2}' = x_i sin + x_{i+D/2} cos.
+// The rounding steps are spelled out (no compiler-chosen contraction), so the
+// result does not depend on how a kernel around it is compiled.
+__device__ __forceinline__ void rope_rotate8(const float (&a)[8], const float (&b)[8], const float (&c)[8],
+                                             const float (&s)[8], float (&ra)[8], float (&rb)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    ra[i] = __fmaf_rn(a[i], c[i], -__fmul_rn(b[i], s[i]));
+    rb[i] = __fmaf_rn(a[i], s[i], __fmul_rn(b[i], c[i]));
+  }
+}
+
 }  // namespace fa

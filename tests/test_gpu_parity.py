@@ -308,10 +308,13 @@ def test_repeated_calls_deterministic(fa, cuda_device):
 
 
 @pytest.mark.parametrize("B,S,Hq,Hk,dtype,theta", [(3, 4096, 8, 2, "bfloat16", 5e5), (1, 8192, 8, 4, "float16", None),
-                                                  (1, 6000, 6, 3, "bfloat16", 1e4)])
+                                                  (1, 6000, 6, 3, "bfloat16", 1e4),
+                                                  (1, 16384, 16, 2, "bfloat16", 5e5),
+                                                  (2, 9000, 32, 8, "float16", 1e4)])
 def test_host_path_chunked_pipeline_matches_device_path(fa, cuda_device, B, S, Hq, Hk, dtype, theta):
-    """Large host-pointer calls are split into batch / KV-head-group chunks whose
-    copies overlap compute; every chunk must equal the device-path result."""
+    """Large host-pointer calls are split into (batch, query-row block) chunks
+    whose copies overlap compute (heaviest block of each batch first); the
+    result must equal the device-path result bit for bit."""
     import torch
 
     tdt = _torch_dtype(dtype)
