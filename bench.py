@@ -7,10 +7,11 @@ one `_flash_attn_metal.forward` call (RoPE/convert pre-pass + attention
 kernel). With --gpus N (torchrun, one process per GPU) every rank runs its
 own batch shard of that size (weak scaling, no collective on the data path);
 value = FLOPs of all ranks / max-over-ranks device time. cfg5b (8 query
-heads over one KV head) instead splits ONE problem across the ranks by key
-range (strong scaling): a step is the partial kernel with its epilogue
-storing into the row owners' staging over NVLink, a one-element NCCL
-barrier, and the owners' merge.
+heads over one KV head) instead splits ONE problem across the ranks (strong
+scaling): by default each rank computes zig-zag query-row chunks against the
+replicated K/V (no merge); with --split kv each rank computes one key range,
+its kernel epilogue stores the partials into the row owners' staging over
+NVLink, and after a one-element NCCL barrier the owners merge.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg4]
     python bench.py --impl reference ...   # the oracle port on the host cores
@@ -50,9 +51,7 @@ CONFIGS = {
     "cfg5b": (1, 65536, 8, 1, 128, "bfloat16", True, 500000.0, 0.5,
               "long-context causal MQA bf16 B1 S65536 Hq8 Hkv1 D128 RoPE 5e5 (split-KV across GPUs)"),
 }
-# Configs whose one problem is split across the ranks (strong scaling):
-# balanced key ranges per rank, partials stored into the row owners' staging
-# over NVLink, merged by the owners.
+# Configs whose one problem is split across the ranks (strong scaling, --split).
 SPLIT_KV = {"cfg5b"}
 
 
@@ -222,8 +221,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
-    ap.add_argument("--split", choices=["kv", "q"], default="kv",
-                    help="how cfg5b is split over ranks: key ranges + merge (kv) or zig-zag query rows (q)")
+    ap.add_argument("--split", choices=["kv", "q"], default="q",
+                    help="how cfg5b is split over ranks: zig-zag query rows with K/V replicated (q, the faster: "
+                         "no merge) or key ranges with partials merged by the row owners (kv)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
