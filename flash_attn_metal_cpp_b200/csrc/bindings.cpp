@@ -87,6 +87,10 @@ void fill_params(fa_params& p, const std::vector<int64_t>& qs, const std::vector
   p.rope_theta = rope_theta;
 }
 
+void check_slopes(int64_t n, int64_t heads_q) {
+  if (n != heads_q) forward_error("alibi_slopes must hold one float32 slope per query head");
+}
+
 void check_shapes(const std::vector<int64_t>& qs, const std::vector<int64_t>& ks,
                   const std::vector<int64_t>& vs) {
   if (qs.size() != 4 || ks.size() != 4 || vs.size() != 4)
@@ -130,6 +134,12 @@ py::object forward_numpy(py::object Q, py::object K, py::object V, float scale, 
   p.dtype = code;
   p.out_dtype = out_code;
   const int oc = out_code < 0 ? code : out_code;
+  py::array slopes;
+  if (!alibi.is_none()) {
+    slopes = np.attr("ascontiguousarray")(alibi, "float32");
+    check_slopes(slopes.size(), qs[2]);
+    p.alibi_slopes = static_cast<const float*>(slopes.data());
+  }
   py::array c_arr, s_arr;
   const float* cp = nullptr;
   const float* sp = nullptr;
@@ -210,6 +220,14 @@ py::object forward_torch(py::object Q, py::object K, py::object V, float scale, 
   p.out_dtype = out_code;
   const int oc = out_code < 0 ? code : out_code;
   py::tuple shape = py::make_tuple(qs[0], qs[1], qs[2], qs[3]);
+  // ALiBi slopes as float32 next to the tensors (host memory for CPU tensors).
+  py::object slopes = py::none();
+  if (!alibi.is_none()) {
+    slopes = torch.attr("as_tensor")(alibi, py::arg("dtype") = torch.attr("float32"),
+                                     py::arg("device") = Q.attr("device")).attr("contiguous")();
+    check_slopes(slopes.attr("numel")().cast<int64_t>(), qs[2]);
+    p.alibi_slopes = reinterpret_cast<const float*>(slopes.attr("data_ptr")().cast<uintptr_t>());
+  }
 
   if (!cuda) {
     // CPU tensors: host path (contiguous), like the NumPy route.

@@ -231,9 +231,8 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
   if (out_dt > 2) return fail(FA_ERR_INVALID_ARG, "out_dtype must be -1, 0, 1 or 2");
   if (p->dropout_p != 0.f)
     return fail(FA_ERR_UNSUPPORTED, "dropout_p != 0 is not supported (the reference kernel ignores it)");
-  if (p->has_alibi) return fail(FA_ERR_UNSUPPORTED, "alibi_slopes are not supported (the reference kernel ignores them)");
-  if (p->window_left != -1 || p->window_right != -1)
-    return fail(FA_ERR_UNSUPPORTED, "window_size is not supported (the reference kernel ignores it)");
+  if (p->has_alibi && p->alibi_slopes == nullptr)
+    return fail(FA_ERR_INVALID_ARG, "has_alibi needs alibi_slopes (float32, one slope per query head)");
   if (p->head_dim == 0 || p->head_dim > 256)
     return fail(FA_ERR_UNSUPPORTED, "head_dim must be in [1, 256]");
   if (p->num_heads_k == 0 || p->num_heads_q % p->num_heads_k != 0)
@@ -258,6 +257,9 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
   a.scale = p->softmax_scale;
   a.scale_log2 = (float)((double)p->softmax_scale * 1.4426950408889634);
   a.causal = p->is_causal ? 1 : 0;
+  a.win_left = p->window_left < 0 ? -1 : p->window_left;
+  a.win_right = p->window_right < 0 ? -1 : p->window_right;
+  a.alibi = p->has_alibi ? p->alibi_slopes : nullptr;
   a.q_begin = 0;
   a.q_end = a.Sq;
   a.kv_begin = 0;
@@ -286,7 +288,10 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
   bool strides_ok = true;
   for (int i = 0; i < 3; ++i)
     strides_ok &= al(qs[i], in_mult) && al(ks[i], in_mult) && al(vs[i], in_mult) && al(os[i], out_mult);
-  pl->tc = (p->dtype == kF16 || p->dtype == kBF16) && (D == 64 || D == 128) && strides_ok;
+  // The tensor-core kernel folds the ALiBi bias into the raw score as
+  // (slope / scale) * (k - q), so a zero scale with ALiBi takes the CUDA-core kernel.
+  pl->tc = (p->dtype == kF16 || p->dtype == kBF16) && (D == 64 || D == 128) && strides_ok &&
+           !(p->has_alibi && p->softmax_scale == 0.f);
   pl->need_q16 = pl->tc && pl->rope;
   pl->need_k16 = pl->tc && pl->rope;
   pl->need_v16 = pl->tc && p->dtype == kBF16;
@@ -726,6 +731,13 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
   }
   const float* tc = tables ? static_cast<const float*>(dc.p) : nullptr;
   const float* tsn = tables ? static_cast<const float*>(dsn.p) : nullptr;
+  // ALiBi slopes arrive in host memory here: stage them next to the tensors.
+  Lease dal(&ds->pool, p->has_alibi ? (size_t)a.Hq * sizeof(float) : 0);
+  if (p->has_alibi) {
+    if (!dal.p) return fail(FA_ERR_CUDA, "device allocation failed");
+    FA_CUDA(cudaMemcpyAsync(dal.p, p->alibi_slopes, (size_t)a.Hq * sizeof(float), cudaMemcpyHostToDevice, s));
+    pl.a.alibi = static_cast<const float*>(dal.p);
+  }
 
   // Pipeline over query-row blocks: for each batch, K and V are copied in
   // first, then Q in blocks of rows, the block with the LAST rows first (under

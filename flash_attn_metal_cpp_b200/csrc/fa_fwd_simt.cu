@@ -100,9 +100,15 @@ __global__ void __launch_bounds__(THREADS)
   const int q_last = min(q0 + ROWS, a.q_end) - 1;
   int kv_hi = a.kv_end;
   if (CAUSAL) kv_hi = min(kv_hi, q_last + 1);
+  if (a.win_right >= 0) kv_hi = min(kv_hi, q_last + a.win_right + 1);
+  // Tiles wholly left of every row's window are skipped (tile starts stay
+  // aligned to kv_begin).
+  int kv_lo = a.kv_begin;
+  if (a.win_left >= 0 && q0 - a.win_left > kv_lo) kv_lo += (q0 - a.win_left - kv_lo) / KT * KT;
+  const float slope = a.alibi ? a.alibi[hq] : 0.f;
 
   float m_run = -INFINITY, l_run = 0.f;
-  for (int kv0 = a.kv_begin; kv0 < kv_hi; kv0 += KT) {
+  for (int kv0 = kv_lo; kv0 < kv_hi; kv0 += KT) {
     __syncthreads();
     for (int e = tid; e < KT * DMAX; e += THREADS) {
       const int kr = e / DMAX, col = e % DMAX;
@@ -129,8 +135,11 @@ __global__ void __launch_bounds__(THREADS)
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       const int key = kv0 + j;
-      const bool vis = key < a.kv_end && (!CAUSAL || key <= row_g);
-      s[j] = vis ? acc * a.scale : -INFINITY;
+      const int rel = key - row_g;  // k - q
+      const bool vis = key < a.kv_end && (!CAUSAL || rel <= 0) && (a.win_left < 0 || rel >= -a.win_left) &&
+                       (a.win_right < 0 || rel <= a.win_right);
+      // scale before the mask (.metal:138-143); ALiBi slope * (k - q) on the scaled score
+      s[j] = vis ? fmaf(slope, (float)rel, acc * a.scale) : -INFINITY;
       mx = fmaxf(mx, s[j]);
     }
     const float m_new = fmaxf(m_run, mx);

@@ -121,7 +121,10 @@ __device__ __forceinline__ void store_row32<float>(float* dst, const float* v) {
   for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
 }
 
-template <int D, bool CAUSAL, bool QK_BF16, typename OutT>
+// EXT: the sliding-window and ALiBi variant (common.metal:95-128). Without
+// it those code paths are compiled out, so the plain kernel keeps its
+// critical path (the per-step softmax) free of their checks.
+template <int D, bool CAUSAL, bool QK_BF16, typename OutT, bool EXT>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_sm100(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const AttnArgs a) {
@@ -147,20 +150,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hk = hq / a.group;
   const int q0 = a.q_begin + blk * NT * BM;
 
-  // KV tiles visited by each query tile (0 for a tile with no row in range).
-  int n_kv_t[NT];
+  // KV tiles of each query tile: absolute tiles [jlo, jhi) counted from
+  // kv_begin in steps of BN. The causal mask and the right side of a sliding
+  // window cap the last tile; the left side of the window skips whole tiles
+  // before the first visible key. The CTA streams tiles [j_min, j_min + n_kv)
+  // through its K/V rings (ring index j); tile t takes part in ring indices
+  // [s_lo[t], s_lo[t] + n_kv_t[t]).
+  int s_lo[NT], n_kv_t[NT];
+  int j_min = 0x7fffffff, j_max = 0;
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
     const int r0 = q0 + t * BM;
-    int n = 0;
+    int lo = 0, hi = 0;
     if (r0 < a.q_end) {
-      int kv_hi = a.kv_end;
-      if (CAUSAL) kv_hi = min(kv_hi, min(r0 + BM, a.q_end));
-      n = (kv_hi > a.kv_begin) ? (kv_hi - a.kv_begin + BN - 1) / BN : 0;
+      const int r_last = min(r0 + BM, a.q_end) - 1;
+      long long kv_hi = a.kv_end;
+      if (CAUSAL) kv_hi = min(kv_hi, (long long)r_last + 1);
+      int kv_lo = a.kv_begin;
+      if constexpr (EXT) {
+        if (a.win_right >= 0) kv_hi = min(kv_hi, (long long)r_last + a.win_right + 1);
+        if (a.win_left >= 0) kv_lo = max(kv_lo, r0 - a.win_left);
+      }
+      if (kv_hi > kv_lo) {
+        lo = EXT ? (kv_lo - a.kv_begin) / BN : 0;
+        hi = (int)((kv_hi - a.kv_begin + BN - 1) / BN);
+      }
     }
-    n_kv_t[t] = n;
+    s_lo[t] = lo;
+    n_kv_t[t] = hi - lo;
+    if (hi > lo) {
+      j_min = min(j_min, lo);
+      j_max = max(j_max, hi);
+    }
   }
-  const int n_kv = max(n_kv_t[0], n_kv_t[1]);
+  if constexpr (!EXT) j_min = 0;  // every tile starts at the first key
+  const int n_kv = (j_max > 0) ? j_max - j_min : 0;
+  if constexpr (EXT) {
+#pragma unroll
+    for (int t = 0; t < NT; ++t) s_lo[t] -= (n_kv > 0) ? j_min : 0;  // ring-relative
+  }
 
   if (threadIdx.x == kProducerWarp * 32) {
 #pragma unroll
@@ -228,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int bx = 0; bx < C::NBOX; ++bx)
           tma_load_4d(ring + st * C::TILE_BYTES + bx * C::BOX_BYTES, tm, bfull, bx * 64, hk,
-                      a.kv_begin + j * BN, bz);
+                      a.kv_begin + (j_min + j) * BN, bz);
         issued = j + 1;
       }
       // Never leave the CTA with bulk copies still writing shared memory.
@@ -262,9 +290,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < NT; ++t) {
           const uint32_t tS = tmem + kColS + t * 128;
           const uint32_t tO = tmem + kColO + t * 128;
-          if (j >= 1 && j - 1 < n_kv_t[t]) {
+          if (j >= 1 && j - 1 >= s_lo[t] && j - 1 < s_lo[t] + n_kv_t[t]) {
             // O_t += P_t V_{j-1}: P from TMEM (first 64 columns of S_t), V MN-major from smem.
             const int i = j - 1;
+            const int it = i - s_lo[t];  // this tile's step
             if (!v_ready) {
               if (!fa_wait(smem_addr(&bars->v_full[i % C::NS]), (i / C::NS) & 1, a.status)) { ok = false; break; }
               v_ready = true;
@@ -275,16 +304,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t v_lo = v_lo0 + (uint32_t)((i % C::NS) * C::TILE_BYTES >> 4);
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
-              if (!fa_wait(smem_addr(&bars->p_full[t][half]), i & 1, a.status)) { ok = false; break; }
+              if (!fa_wait(smem_addr(&bars->p_full[t][half]), it & 1, a.status)) { ok = false; break; }
               tc_fence_after();
 #pragma unroll
               for (int kk = half * 4; kk < half * 4 + 4; ++kk)
-                mma_ts_lohi(tO, tS + kk * 8, v_lo + kk * (16 * 128 >> 4), v_hi, idesc_o, (i > 0 || kk > 0) ? 1u : 0u);
+                mma_ts_lohi(tO, tS + kk * 8, v_lo + kk * (16 * 128 >> 4), v_hi, idesc_o, (it > 0 || kk > 0) ? 1u : 0u);
             }
             if (!ok) break;
-            if (i == n_kv_t[t] - 1) mma_commit(smem_addr(&bars->o_full[t]));
+            if (it == n_kv_t[t] - 1) mma_commit(smem_addr(&bars->o_full[t]));
           }
-          if (j < n_kv_t[t]) {
+          if (j >= s_lo[t] && j < s_lo[t] + n_kv_t[t]) {
             // S_t = Q_t K_j^T.
             if (!k_ready) {
               if (!fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status)) { ok = false; break; }
@@ -316,7 +345,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp >> 2;               // query tile of this warpgroup
     const int row = threadIdx.x & 127;     // TMEM lane
     const int row_g = q0 + t * BM + row;
-    const int my_kv = n_kv_t[t];
+    const int my_kv = (t == 0) ? n_kv_t[0] : n_kv_t[1];  // t is not a constant here
+    const int my_lo = EXT ? j_min + ((t == 0) ? s_lo[0] : s_lo[1]) : 0;  // absolute first KV tile
+    const int r_tile = q0 + t * BM;
+    // ALiBi (common.metal:123-128): slope * (k - q) on the scaled score, folded
+    // into the raw score as (slope / scale) * (k - q) (scale != 0 on this path).
+    const float slope_raw = (EXT && a.alibi != nullptr) ? a.alibi[hq] / a.scale : 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t tS = lane_base + kColS + t * 128;
     const uint32_t tO = lane_base + kColO + t * 128;
@@ -335,21 +369,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       float s[BN];
       tmem_ld128(tS, s);
 
-      const int kv0 = a.kv_begin + j * BN;
-      const bool need_mask = (kv0 + BN > a.kv_end) || (CAUSAL && kv0 + BN - 1 > q0 + t * BM);
-      int key_lim = a.kv_end - kv0;                       // keys [kv0, kv0+key_lim) visible
+      const int kv0 = a.kv_begin + (my_lo + j) * BN;
+      bool need_mask = (kv0 + BN > a.kv_end) || (CAUSAL && kv0 + BN - 1 > r_tile);
+      int key_lim = a.kv_end - kv0;                       // keys [kv0 + key_beg, kv0 + key_lim) visible
       if (CAUSAL) key_lim = min(key_lim, row_g - kv0 + 1);
+      int key_beg = -1;
+      if constexpr (EXT) {
+        need_mask = need_mask || (a.win_right >= 0 && kv0 + BN - 1 > r_tile + a.win_right) ||
+                    (a.win_left >= 0 && kv0 < r_tile + BM - 1 - a.win_left);
+        if (a.win_right >= 0) key_lim = (int)min((long long)key_lim, (long long)row_g + a.win_right - kv0 + 1);
+        if (a.win_left >= 0) key_beg = row_g - a.win_left - kv0;
+        if (a.alibi != nullptr) {
+          const float base = (float)(kv0 - row_g);
+#pragma unroll
+          for (int c = 0; c < BN; ++c) s[c] = fmaf(slope_raw, base + (float)c, s[c]);
+        }
+      }
       float ext;
       if (!need_mask && sl2 > 0.f) {
         ext = row_max128(s);  // hot path: full tile, positive scale
       } else if (sl2 >= 0.f) {
         ext = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) ext = fmaxf(ext, (!need_mask || c < key_lim) ? s[c] : -INFINITY);
+        for (int c = 0; c < BN; ++c) ext = fmaxf(ext, (!need_mask || (c < key_lim && c >= key_beg)) ? s[c] : -INFINITY);
       } else {
         ext = INFINITY;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) ext = fminf(ext, (!need_mask || c < key_lim) ? s[c] : INFINITY);
+        for (int c = 0; c < BN; ++c) ext = fminf(ext, (!need_mask || (c < key_lim && c >= key_beg)) ? s[c] : INFINITY);
       }
       const float m_cand = (sl2 == 0.f) ? 0.f : ext * sl2;
       const float m_new = fmaxf(m_run, m_cand);
@@ -379,8 +425,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int c = c0 + 2 * i;
-            const float p0 = (c < key_lim) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
-            const float p1 = (c + 1 < key_lim) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
+            const float p0 = (c < key_lim && c >= key_beg) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
+            const float p1 = (c + 1 < key_lim && c + 1 >= key_beg) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
             acc0 = __fadd2_rn(acc0, make_float2(p0, p1));
             p[i] = pack_half2(p0, p1);
           }
@@ -462,7 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int D, bool CAUSAL, bool QK_BF16, typename OutT>
 cudaError_t launch_t(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap& tk,
                      const CUtensorMap& tv, cudaStream_t stream) {
-  auto kern = attn_fwd_sm100<D, CAUSAL, QK_BF16, OutT>;
+  const bool ext = a.win_left >= 0 || a.win_right >= 0 || a.alibi != nullptr;
+  auto kern = ext ? attn_fwd_sm100<D, CAUSAL, QK_BF16, OutT, true> : attn_fwd_sm100<D, CAUSAL, QK_BF16, OutT, false>;
   constexpr int smem = Cfg<D>::SMEM_BYTES;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -16,6 +16,9 @@ struct AttnArgs {
   float scale;             // softmax_scale as given
   float scale_log2;        // softmax_scale * log2(e)
   int causal;              // top-left causal mask: key k masked for query q iff k > q
+  int win_left, win_right; // sliding window: key k masked iff k - q < -win_left (win_left >= 0)
+                           // or k - q > win_right (win_right >= 0); negative = unbounded
+  const float* alibi;      // [Hq] slopes: slope[h] * (k - q) added to the scaled score (NULL = none)
   int q_begin, q_end;      // query rows computed (partial API); [0, Sq) otherwise
   int kv_begin, kv_end;    // keys visited (split-KV); [0, Sk) otherwise
   int n_q_tiles;           // tiles of the query range for the launch

@@ -82,10 +82,12 @@ typedef struct fa_params {
     uint32_t head_dim;
     float softmax_scale;      /* used as given; 0 gives uniform weights, as in the reference */
     int32_t is_causal;
-    int32_t window_left;      /* -1 = none; any other value is rejected (UNSUPPORTED) */
-    int32_t window_right;     /* -1 = none; any other value is rejected (UNSUPPORTED) */
+    int32_t window_left;      /* sliding window (common.metal:95-104): key k is masked for */
+    int32_t window_right;     /* query q if k - q < -window_left or k - q > window_right;
+                                 a negative value leaves that side unbounded (-1 = none) */
     float dropout_p;          /* must be 0 (UNSUPPORTED otherwise) */
-    int32_t has_alibi;        /* must be 0 (UNSUPPORTED otherwise) */
+    int32_t has_alibi;        /* add alibi_slopes[h] * (k - q) to the scaled scores
+                                 (common.metal:123-128); needs alibi_slopes */
     int32_t has_rotary;       /* apply rotate-half RoPE to Q and K */
     uint32_t gqa_group_size;  /* 0 = derive num_heads_q / num_heads_k; else must equal it */
 
@@ -99,6 +101,10 @@ typedef struct fa_params {
     int64_t k_stride[3];
     int64_t v_stride[3];
     int64_t o_stride[3];
+    /* float32 [num_heads_q] ALiBi slopes when has_alibi: device memory for
+     * fa_forward / fa_forward_range / fa_forward_partial / fa_forward_noalloc,
+     * host memory for fa_forward_host. */
+    const float* alibi_slopes;
 } fa_params;
 
 /* Fill `p` with the reference defaults (scale 0, no mask, no RoPE, contiguous). */

@@ -20,6 +20,12 @@ plus the parts of the path the reference only declares:
                              reference host binds (src/flash_attn_core.cpp:343-349),
                              angle(pos, i) = pos * theta^(-2i/D) computed in float64
   * gqa head map             common.metal:215-217 (kv_head = q_head // group)
+  * sliding-window mask      common.metal:95-104 (key k masked for query q iff
+                             window_left >= 0 and k - q < -window_left, or
+                             window_right >= 0 and k - q > window_right;
+                             combined with the causal mask, :107-119)
+  * ALiBi bias               common.metal:123-128 (slope[h] * (k - q) added to
+                             the scaled score)
 and the split-KV partial / (O, LSE) combine used by the multi-GPU path.
 
 Pinning: attention_ref / torch_attention_reference are checked against
@@ -80,8 +86,14 @@ def attention_ref(
     compute_dtype=np.float32,
     kv_range: Optional[Tuple[int, int]] = None,
     q_range: Optional[Tuple[int, int]] = None,
+    window: Optional[Tuple[int, int]] = None,
+    alibi_slopes: Optional[np.ndarray] = None,
 ):
     """NumPy restatement of test.py:39-93 `attention_ref`.
+
+    window=(left, right) adds the sliding-window mask of common.metal:95-104
+    (a negative side is unbounded); alibi_slopes (Hq,) adds
+    slope[h] * (k - q) to the scaled scores (common.metal:123-128).
 
     q: (B, Sq, Hq, D), k/v: (B, Sk, Hk, D), any float dtype (values are
     taken exactly, then computed in `compute_dtype`, float32 by default as
@@ -121,8 +133,17 @@ def attention_ref(
                 r1 = min(r0 + q_block, r_hi)
                 s = _scores_block(qf[b, r0:r1, h, :], k_bh, softmax_scale)
                 vis = (keys[None, :] >= k_lo) & (keys[None, :] < k_hi)
+                rel = keys[None, :] - np.arange(r0, r1)[:, None]  # k - q
                 if causal:  # top-left: key k masked for query q iff k > q (triu diagonal=1)
-                    vis = vis & (keys[None, :] <= np.arange(r0, r1)[:, None])
+                    vis = vis & (rel <= 0)
+                if window is not None:  # common.metal:95-104
+                    wl, wr = window
+                    if wl >= 0:
+                        vis = vis & (rel >= -wl)
+                    if wr >= 0:
+                        vis = vis & (rel <= wr)
+                if alibi_slopes is not None:  # common.metal:123-128
+                    s = s + (np.float32(alibi_slopes[h]) * rel.astype(np.float32)).astype(cd)
                 vis = np.broadcast_to(vis, s.shape)
                 s = np.where(vis, s, -np.inf)
                 m = s.max(axis=1, keepdims=True)

@@ -294,8 +294,8 @@ def test_errors_are_runtime_errors(fa, cuda_device):
         fa.forward(q, k, k, softmax_scale=0.1)  # 4 query heads, 3 kv heads
     with pytest.raises(RuntimeError, match="dropout"):
         fa.forward(q, q, q, softmax_scale=0.1, dropout_p=0.1)
-    with pytest.raises(RuntimeError, match="window"):
-        fa.forward(q, q, q, softmax_scale=0.1, window_size=(4, 0))
+    with pytest.raises(RuntimeError, match="alibi_slopes must hold one"):
+        fa.forward(q, q, q, softmax_scale=0.1, alibi_slopes=torch.ones(3))
 
 
 def test_repeated_calls_deterministic(fa, cuda_device):

@@ -64,8 +64,8 @@ def test_forward_validation_errors(fam):
         fam.forward(x.astype(np.int16), x.astype(np.int16), x.astype(np.int16))
     with pytest.raises(RuntimeError, match="dropout"):
         fam.forward(x, x, x, 0.1, False, 0.5)
-    with pytest.raises(RuntimeError, match="alibi"):
-        fam.forward(x, x, x, 0.1, False, 0.0, np.ones(2, np.float32))
+    with pytest.raises(RuntimeError, match="alibi_slopes must hold one"):
+        fam.forward(x, x, x, 0.1, False, 0.0, np.ones(3, np.float32))  # 2 query heads
 
 
 def test_package_wrapper(fam):

@@ -103,3 +103,35 @@ def test_empty_keys_and_uniform_scale():
 
 def test_flop_count_convention():
     assert orc.attention_flops(4, 8192, 8192, 32, 128, True) == 4 * 4 * 32 * 8192 * 8192 * 128 / 2
+
+
+@pytest.mark.parametrize("causal,window,alibi", [(True, (7, -1), True), (False, (5, 3), False),
+                                                 (False, None, True), (True, (-1, -1), False)])
+def test_window_and_alibi_match_dense_formula(causal, window, alibi):
+    """Sliding window (common.metal:95-104) and ALiBi (common.metal:123-128)
+    against a dense torch evaluation of the same formulas."""
+    import torch
+
+    rng = np.random.default_rng(11)
+    B, Sq, Sk, H, D = 2, 37, 45, 3, 16
+    q = rng.standard_normal((B, Sq, H, D), dtype=np.float32)
+    k = rng.standard_normal((B, Sk, H, D), dtype=np.float32)
+    v = rng.standard_normal((B, Sk, H, D), dtype=np.float32)
+    sl = np.array([0.5, 0.25, 0.125], np.float32) if alibi else None
+    got = orc.attention_ref(q, k, v, causal=causal, softmax_scale=0.3, window=window, alibi_slopes=sl, q_block=8)
+    qt, kt, vt = (torch.from_numpy(x).permute(0, 2, 1, 3).double() for x in (q, k, v))
+    s = qt @ kt.transpose(-1, -2) * 0.3
+    rel = (torch.arange(Sk)[None, :] - torch.arange(Sq)[:, None]).double()
+    if alibi:
+        s = s + torch.from_numpy(sl).double()[None, :, None, None] * rel
+    mask = torch.zeros(Sq, Sk, dtype=torch.bool)
+    if causal:
+        mask |= rel > 0
+    if window is not None and window[0] >= 0:
+        mask |= rel < -window[0]
+    if window is not None and window[1] >= 0:
+        mask |= rel > window[1]
+    s = s.masked_fill(mask, -float("inf"))
+    p = torch.softmax(s, -1).nan_to_num(0.0)
+    ref = (p @ vt).permute(0, 2, 1, 3).numpy()
+    np.testing.assert_allclose(got, ref, atol=2e-6)

@@ -35,6 +35,7 @@ class FaParams(ctypes.Structure):
         ("out_dtype", ctypes.c_int32), ("rope_theta", ctypes.c_float),
         ("q_stride", ctypes.c_int64 * 3), ("k_stride", ctypes.c_int64 * 3),
         ("v_stride", ctypes.c_int64 * 3), ("o_stride", ctypes.c_int64 * 3),
+        ("alibi_slopes", ctypes.c_void_p),
     ]
 
 
