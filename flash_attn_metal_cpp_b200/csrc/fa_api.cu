@@ -208,6 +208,8 @@ struct Plan {
   bool tc;          // tensor-core path
   bool rope;
   bool need_q16, need_k16, need_v16;   // operands staged as fp16 in the workspace
+  bool pad;         // head dim padded with zeros to d_pad for the tensor-core kernel
+  int d_pad;
   float rope_theta;
   size_t ws_bytes;
 };
@@ -290,8 +292,14 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
     strides_ok &= al(qs[i], in_mult) && al(ks[i], in_mult) && al(vs[i], in_mult) && al(os[i], out_mult);
   // The tensor-core kernel folds the ALiBi bias into the raw score as
   // (slope / scale) * (k - q), so a zero scale with ALiBi takes the CUDA-core kernel.
-  pl->tc = (p->dtype == kF16 || p->dtype == kBF16) && (D == 64 || D == 128) && strides_ok &&
-           !(p->has_alibi && p->softmax_scale == 0.f);
+  const bool tc_ok = (p->dtype == kF16 || p->dtype == kBF16) && !(p->has_alibi && p->softmax_scale == 0.f);
+  // Head dims 64 and 128 run natively (operands zero-copy when 16-byte
+  // aligned); any other head dim <= 128 is zero-padded to 64 or 128 by the
+  // staging pass (padding adds zero terms to every dot product) and the first
+  // D columns of the padded output are copied out.
+  pl->tc = tc_ok && (D == 64 || D == 128) && strides_ok;
+  pl->pad = tc_ok && !pl->tc && D < 128 && D != 64;
+  pl->d_pad = D <= 64 ? 64 : 128;
   pl->need_q16 = pl->tc && pl->rope;
   pl->need_k16 = pl->tc && pl->rope;
   pl->need_v16 = pl->tc && p->dtype == kBF16;
@@ -300,6 +308,11 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
   if (pl->need_q16) ws += up((size_t)a.B * a.Sq * a.Hq * D * 2);
   if (pl->need_k16) ws += up((size_t)a.B * a.Sk * a.Hk * D * 2);
   if (pl->need_v16) ws += up((size_t)a.B * a.Sk * a.Hk * D * 2);
+  if (pl->pad) {
+    const size_t dp = (size_t)pl->d_pad;
+    ws = up((size_t)a.B * a.Sq * a.Hq * dp * 2) + 2 * up((size_t)a.B * a.Sk * a.Hk * dp * 2) +
+         up((size_t)a.B * a.Sq * a.Hq * dp * dtype_size(out_dt));
+  }
   pl->ws_bytes = ws;
   return FA_OK;
 }
@@ -388,6 +401,77 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     if (st != FA_OK) return st;
   }
   if (!pl.rope) cs = sn = nullptr;
+
+  if (pl.pad) {
+    // Head dim D -> d_pad: Q, K, V staged zero-padded (RoPE applied on the
+    // original D's pairs), the tensor-core kernel writes a padded O into the
+    // workspace, and its first D columns are copied to the caller's O.
+    if (a.route_rows > 0) return fail(FA_ERR_UNSUPPORTED, "routed output needs head_dim 64 or 128");
+    if (workspace == nullptr) {
+      fa_status st = stream_workspace(ds, stream, pl.ws_bytes, &workspace);
+      if (st != FA_OK) return st;
+    } else if (ws_bytes < pl.ws_bytes) {
+      return fail(FA_ERR_INVALID_ARG, "workspace smaller than fa_workspace_size()");
+    }
+    const int Dp = pl.d_pad;
+    uint8_t* wp = static_cast<uint8_t*>(workspace);
+    auto take = [&](size_t bytes) {
+      uint8_t* r = wp;
+      wp += (bytes + 255) & ~size_t(255);
+      return r;
+    };
+    __half* q16 = reinterpret_cast<__half*>(take((size_t)a.B * a.Sq * a.Hq * Dp * 2));
+    __half* k16 = reinterpret_cast<__half*>(take((size_t)a.B * a.Sk * a.Hk * Dp * 2));
+    __half* v16 = reinterpret_cast<__half*>(take((size_t)a.B * a.Sk * a.Hk * Dp * 2));
+    void* opad = take((size_t)a.B * a.Sq * a.Hq * Dp * dtype_size(pl.out_dtype));
+    const size_t esz = dtype_size(pl.dtype);
+    const int q_lo = a.q_begin, q_hi = std::min(a.Sq, a.q_begin + (a.q_end - a.q_begin + 127) / 128 * 128);
+    const int k_lo = a.kv_begin, k_hi = std::min(a.Sk, a.kv_begin + (a.kv_end - a.kv_begin + 127) / 128 * 128);
+    const int hd = a.D / 2;
+    cudaError_t e = launch_prep_pad(static_cast<const uint8_t*>(q) + (size_t)q_lo * a.q_ss * esz, pl.dtype, a.q_sb,
+                                    a.q_ss, a.q_sh, a.B, q_hi - q_lo, a.Hq, a.D, Dp,
+                                    cs ? cs + (size_t)q_lo * hd : nullptr, sn ? sn + (size_t)q_lo * hd : nullptr,
+                                    q16 + (size_t)q_lo * a.Hq * Dp, a.Sq, ds->status, stream);
+    if (e == cudaSuccess)
+      e = launch_prep_pad(static_cast<const uint8_t*>(k) + (size_t)k_lo * a.k_ss * esz, pl.dtype, a.k_sb, a.k_ss,
+                          a.k_sh, a.B, k_hi - k_lo, a.Hk, a.D, Dp, cs ? cs + (size_t)k_lo * hd : nullptr,
+                          sn ? sn + (size_t)k_lo * hd : nullptr, k16 + (size_t)k_lo * a.Hk * Dp, a.Sk, ds->status,
+                          stream);
+    if (e == cudaSuccess)
+      e = launch_prep_pad(static_cast<const uint8_t*>(v) + (size_t)k_lo * a.v_ss * esz, pl.dtype, a.v_sb, a.v_ss,
+                          a.v_sh, a.B, k_hi - k_lo, a.Hk, a.D, Dp, nullptr, nullptr,
+                          v16 + (size_t)k_lo * a.Hk * Dp, a.Sk, ds->status, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "padded staging");
+    AttnArgs ap = a;
+    ap.D = Dp;
+    ap.o = opad;
+    ap.o_ss = (int64_t)a.Hq * Dp;
+    ap.o_sh = Dp;
+    ap.o_sb = (int64_t)a.Sq * ap.o_ss;
+    ap.n_q_tiles = (a.q_end - a.q_begin + 127) / 128;
+    CUtensorMap tq, tk, tv;
+    const int64_t qsb = (int64_t)a.Sq * a.Hq * Dp, qss = (int64_t)a.Hq * Dp;
+    const int64_t ksb = (int64_t)a.Sk * a.Hk * Dp, kss = (int64_t)a.Hk * Dp;
+    fa_status st = encode_map(&tq, q16, false, Dp, a.Hq, a.Sq, a.B, qsb, qss, Dp);
+    if (st == FA_OK) st = encode_map(&tk, k16, false, Dp, a.Hk, a.Sk, a.B, ksb, kss, Dp);
+    if (st == FA_OK) st = encode_map(&tv, v16, false, Dp, a.Hk, a.Sk, a.B, ksb, kss, Dp);
+    if (st != FA_OK) return st;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    if (g_timing) {
+      FA_CUDA(cudaEventCreate(&ev0));
+      FA_CUDA(cudaEventCreate(&ev1));
+      FA_CUDA(cudaEventRecord(ev0, stream));
+    }
+    e = launch_attn_sm100(ap, tq, tk, tv, false, pl.out_dtype, stream);
+    if (g_timing) {
+      FA_CUDA(cudaEventRecord(ev1, stream));
+      g_events.emplace_back(ev0, ev1);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "attention (tensor-core kernel, padded head dim)");
+    e = launch_unpad(opad, a.o, (int)dtype_size(pl.out_dtype), a.o_sb, a.o_ss, a.o_sh, a.B, a.Sq, a.Hq, a.D, Dp,
+                     a.q_begin, a.q_end, stream);
+    return e == cudaSuccess ? FA_OK : cuda_fail(e, "unpad output");
+  }
 
   if (!pl.tc) {
     a.q = q;
@@ -998,6 +1082,10 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
   fa_status st = make_plan(p, &pl);
   if (st != FA_OK) return st;
   AttnArgs& a = pl.a;
+  if (pl.pad) {  // no padded staging here: other head dims take the CUDA-core kernel
+    pl.pad = false;
+    pl.ws_bytes = 0;
+  }
   const bool tables_from_theta = pl.rope && (cos == nullptr || sin == nullptr);
   const int rows = a.Sq > a.Sk ? a.Sq : a.Sk;
   const size_t table_bytes = tables_from_theta ? up256((size_t)rows * (a.D / 2) * sizeof(float)) : 0;

@@ -229,7 +229,118 @@ __global__ void fill_empty_kernel(const AttnArgs a) {
   }
 }
 
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p);
+template <>
+__device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+
+// Zero-padded fp16 staging for head dims the tensor-core kernel does not take
+// natively: y[.., 0:D] = rope(x) with the pairs (i, i + D/2) of the ORIGINAL
+// D (an odd D's last column has no partner and is kept, as in the oracle),
+// y[.., D:Dp] = 0, so every dot product is unchanged. One thread per output
+// element of rows [0, S); y is contiguous [B, y_rows, H, Dp].
+template <typename T>
+__global__ void prep_pad_kernel(const T* __restrict__ x, int64_t sb, int64_t ss, int64_t sh, int S, int H, int D,
+                                int Dp, long long n_rows, const float* __restrict__ cs,
+                                const float* __restrict__ sn, __half* __restrict__ y, int y_rows,
+                                unsigned* status) {
+  const long long total = n_rows * Dp;
+  const int half = D / 2;
+  bool ok = true;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int col = (int)(idx % Dp);
+    const long long rowi = idx / Dp;
+    const int h = (int)(rowi % H);
+    const long long bs = rowi / H;
+    const int s = (int)(bs % S);
+    const int b = (int)(bs / S);
+    const T* src = x + (int64_t)b * sb + (int64_t)s * ss + (int64_t)h * sh;
+    float val = 0.f;
+    if (col < D) {
+      val = ld_f<T>(src + col);
+      if (cs != nullptr && col < 2 * half) {
+        const int i = col < half ? col : col - half;  // pair index
+        const float c = cs[(int64_t)s * half + i], sv = sn[(int64_t)s * half + i];
+        const float a0 = ld_f<T>(src + i), a1 = ld_f<T>(src + i + half);
+        // same rounding steps as rope_rotate8
+        val = (col < half) ? __fmaf_rn(a0, c, -__fmul_rn(a1, sv)) : __fmaf_rn(a0, sv, __fmul_rn(a1, c));
+      }
+      ok &= fabsf(val) <= 65504.f;
+    }
+    y[(((int64_t)b * y_rows + s) * H + h) * Dp + col] = __float2half_rn(val);
+  }
+  if (!ok) atomicOr(status, FA_DEV_RANGE);
+}
+
+// O[b, q, h, 0:D] = O_pad[b, q, h, 0:D] for rows [q_begin, q_end); O_pad is
+// contiguous [B, Sq, H, Dp], O has element strides (sb, ss, sh). Element size
+// 2 or 4 bytes (the output dtype).
+template <typename E>
+__global__ void unpad_kernel(const E* __restrict__ src, E* __restrict__ dst, int64_t sb, int64_t ss, int64_t sh,
+                             int B, int Sq, int H, int D, int Dp, int q_begin, int q_end) {
+  const int nq = q_end - q_begin;
+  const long long total = (long long)B * nq * H * D;
+  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(idx % D);
+    const long long r = idx / D;
+    const int h = (int)(r % H);
+    const long long bq = r / H;
+    const int q = q_begin + (int)(bq % nq);
+    const int b = (int)(bq / nq);
+    dst[(int64_t)b * sb + (int64_t)q * ss + (int64_t)h * sh + d] = src[(((int64_t)b * Sq + q) * H + h) * Dp + d];
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_prep_pad(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H,
+                            int D, int Dp, const float* cs, const float* sn, __half* y, int y_rows, unsigned* status,
+                            cudaStream_t st) {
+  const long long n_rows = (long long)B * S * H;
+  const long long total = n_rows * Dp;
+  if (total == 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  switch (in_dtype) {
+    case kF16:
+      prep_pad_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const __half*>(x), sb, ss, sh, S,
+                                                                H, D, Dp, n_rows, cs, sn, y, y_rows, status);
+      break;
+    case kBF16:
+      prep_pad_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+          reinterpret_cast<const __nv_bfloat16*>(x), sb, ss, sh, S, H, D, Dp, n_rows, cs, sn, y, y_rows, status);
+      break;
+    default:
+      prep_pad_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const float*>(x), sb, ss, sh, S,
+                                                               H, D, Dp, n_rows, cs, sn, y, y_rows, status);
+      break;
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t launch_unpad(const void* src, void* dst, int elem_bytes, int64_t sb, int64_t ss, int64_t sh, int B,
+                         int Sq, int H, int D, int Dp, int q_begin, int q_end, cudaStream_t st) {
+  const long long total = (long long)B * (q_end - q_begin) * H * D;
+  if (total <= 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (elem_bytes == 4)
+    unpad_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst),
+                                                           sb, ss, sh, B, Sq, H, D, Dp, q_begin, q_end);
+  else
+    unpad_kernel<uint16_t><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const uint16_t*>(src),
+                                                              static_cast<uint16_t*>(dst), sb, ss, sh, B, Sq, H, D,
+                                                              Dp, q_begin, q_end);
+  note_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B,
                              int S, int H, int D, const float* cs, const float* sn, __half* y,

@@ -92,6 +92,17 @@ cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss
                              int B, int S, int H, int D, const float* cos, const float* sin,
                              __half* y, int y_rows, unsigned* status, cudaStream_t stream);
 
+// Zero-padded fp16 staging (head dim D -> Dp in {64, 128}) with RoPE on the
+// original D's pairs; y is contiguous [B, y_rows, H, Dp].
+cudaError_t launch_prep_pad(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H,
+                            int D, int Dp, const float* cos, const float* sin, __half* y, int y_rows,
+                            unsigned* status, cudaStream_t stream);
+
+// Copy the first D of Dp columns of a contiguous padded O into O (strides in
+// elements), rows [q_begin, q_end); elem_bytes 2 or 4.
+cudaError_t launch_unpad(const void* src, void* dst, int elem_bytes, int64_t sb, int64_t ss, int64_t sh, int B,
+                         int Sq, int H, int D, int Dp, int q_begin, int q_end, cudaStream_t stream);
+
 // cos/sin tables [rows, D/2] in float32 from theta, computed in double.
 cudaError_t launch_rope_table(float* cos, float* sin, int rows, int D, double theta,
                               cudaStream_t stream);

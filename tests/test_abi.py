@@ -64,7 +64,11 @@ def test_workspace_size_per_path():
     assert ws(0, True) == q16 + kv16              # fp16 + RoPE: rotated Q, K
     assert ws(1, True) == q16 + 2 * kv16          # bf16 + RoPE: Q, K, V
     assert ws(2, True) == 0                       # fp32: CUDA-core kernel, RoPE on load
-    assert ws(0, True, D=96) == 0                 # other head dims: CUDA-core kernel
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    q128, kv128 = 2 * 1000 * 8 * 128 * 2, 2 * 1000 * 2 * 128 * 2
+    assert ws(0, True, D=96) == up(q128) + 2 * up(kv128) + up(q128)  # padded to 128: Q, K, V and O
+    assert ws(1, False, D=40) == up(q128 // 2) + 2 * up(kv128 // 2) + up(q128 // 2)  # padded to 64
+    assert ws(0, True, D=160) == 0                # head dims above 128: CUDA-core kernel
 
 
 def test_rope_tables_match_oracle():

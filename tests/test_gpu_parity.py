@@ -330,3 +330,36 @@ def test_host_path_chunked_pipeline_matches_device_path(fa, cuda_device, B, S, H
     if dtype == "float16":
         out_np = fa.forward(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), softmax_scale=0.09, is_causal=True, **kw)
         assert np.array_equal(out_np, ref.cpu().numpy())
+
+
+@pytest.mark.parametrize("D", [32, 40, 59, 80, 96, 111])
+@pytest.mark.parametrize("dtype,causal", [("float16", False), ("bfloat16", True)])
+def test_odd_head_dims_padded_onto_tensor_cores(fa, cuda_device, D, dtype, causal):
+    """Head dims of the reference's test groups (test.py:293-309,351-368) on
+    16-bit inputs run zero-padded on the tensor-core kernel (staging, kernel,
+    copy-out: several launches) and match the oracle; with RoPE from cos/sin
+    tables, an odd D keeps its last column unrotated."""
+    import torch
+
+    q, k, v = _inputs((2, 333, 4, D), (2, 333, 2, D), _torch_dtype(dtype), seed=D)
+    kw = {}
+    if D % 2 == 1 or D == 80:
+        cs, sn = orc.rope_tables(333, D, 10000.0)
+        kw = {"cos": torch.from_numpy(cs), "sin": torch.from_numpy(sn)}
+    n0 = fa.launch_count()
+    out, lse = fa.forward(q, k, v, softmax_scale=1 / math.sqrt(D), is_causal=causal, out_dtype="float32",
+                          return_lse=True, **kw)
+    torch.cuda.synchronize()
+    fa.check_status()
+    assert fa.launch_count() - n0 >= 5, "expected the padded tensor-core path (staging + kernel + copy-out)"
+    qn, kn, vn = (x.float().cpu().numpy() for x in (q, k, v))
+    if kw:
+        ref, ref_l = orc.attention_with_rope(qn, kn, vn, causal, 1 / math.sqrt(D), cos=cs, sin=sn, return_lse=True)
+    else:
+        ref, ref_l = orc.attention_ref(qn, kn, vn, causal=causal, softmax_scale=1 / math.sqrt(D), return_lse=True)
+    assert_close_16(out.cpu().numpy(), ref, f"D{D} {dtype}")
+    assert np.abs(lse.cpu().numpy() - ref_l).max() <= 1e-3
+    # the host-pointer path gives the same numbers
+    out_h = fa.forward(q.cpu(), k.cpu(), v.cpu(), softmax_scale=1 / math.sqrt(D), is_causal=causal,
+                       out_dtype="float32", **kw)
+    assert np.array_equal(out_h.numpy(), out.cpu().numpy())
