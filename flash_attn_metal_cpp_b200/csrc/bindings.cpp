@@ -414,7 +414,7 @@ void py_forward_range(py::object Q, py::object K, py::object V, std::pair<int64_
 // [B, >= q_range end, Hq, D] (any of the three dtypes, unit innermost
 // stride) and optionally lse [B, Hq, Sq].
 void py_combine(py::object o_parts, py::object lse_parts, py::object out, py::object lse,
-                py::object q_range) {
+                py::object q_range, py::object row_begin) {
   require_cuda(o_parts, "o_parts");
   require_cuda(lse_parts, "lse_parts");
   require_cuda(out, "out");
@@ -461,8 +461,16 @@ void py_combine(py::object o_parts, py::object lse_parts, py::object out, py::ob
   const py::object dev = out.attr("device");
   fa_status st = fa_init(dev.attr("index").is_none() ? 0 : dev.attr("index").cast<int>());
   if (st != FA_OK) forward_error(err_text(st));
-  st = fa_combine(&p, tptr<const float>(o_parts), tptr<const float>(lse_parts), (int32_t)os[0], tptr<void>(out),
-                  lp, (uint32_t)q0, (uint32_t)q1, current_stream_of(out));
+  const int32_t* rb = nullptr;
+  if (!row_begin.is_none()) {
+    require_cuda(row_begin, "row_begin");
+    if (row_begin.attr("numel")().cast<int64_t>() != os[0] ||
+        py::str(row_begin.attr("dtype")).cast<std::string>() != "torch.int32")
+      forward_error("row_begin must be an int32 CUDA tensor with one entry per partial");
+    rb = tptr<const int32_t>(row_begin);
+  }
+  st = fa_combine_ranges(&p, tptr<const float>(o_parts), tptr<const float>(lse_parts), (int32_t)os[0], rb,
+                         tptr<void>(out), lp, (uint32_t)q0, (uint32_t)q1, current_stream_of(out));
   if (st != FA_OK) forward_error(err_text(st));
 }
 
@@ -588,8 +596,9 @@ PYBIND11_MODULE(_flash_attn_metal, m) {
         py::arg("route") = py::none(), py::arg("n_owners") = 0, py::arg("owner_rows") = 0,
         "Rows q_range of the attention over keys kv_range (CUDA tensors, current stream)");
   m.def("combine", &py_combine, py::arg("o_parts"), py::arg("lse_parts"), py::arg("out"),
-        py::arg("lse") = py::none(), py::arg("q_range") = py::none(),
-        "Merge split-KV partials (O_j, LSE_j) into out (CUDA tensors, current stream)");
+        py::arg("lse") = py::none(), py::arg("q_range") = py::none(), py::arg("row_begin") = py::none(),
+        "Merge split-KV partials (O_j, LSE_j) into out (CUDA tensors, current stream); row_begin (int32 "
+        "CUDA tensor, one per partial): rows before it ignore that partial");
   m.def("ipc_alloc", &py_ipc_alloc, py::arg("bytes"),
         "Allocate device memory shareable with other processes: (address, 64-byte handle)");
   m.def("ipc_open", &py_ipc_open, py::arg("handle"), "Map a peer process's allocation; returns its address");

@@ -687,6 +687,12 @@ fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k, c
 
 fa_status fa_combine(const fa_params* p, const float* o_parts, const float* lse_parts, int32_t n_splits,
                      void* o, float* lse, uint32_t q_begin, uint32_t q_end, void* stream) {
+  return fa_combine_ranges(p, o_parts, lse_parts, n_splits, nullptr, o, lse, q_begin, q_end, stream);
+}
+
+fa_status fa_combine_ranges(const fa_params* p, const float* o_parts, const float* lse_parts, int32_t n_splits,
+                            const int32_t* part_row_begin, void* o, float* lse, uint32_t q_begin, uint32_t q_end,
+                            void* stream) {
   Plan pl;
   fa_status st = make_plan(p, &pl);
   if (st != FA_OK) return st;
@@ -699,7 +705,8 @@ fa_status fa_combine(const fa_params* p, const float* o_parts, const float* lse_
   pl.a.q_end = (int)q_end;
   pl.a.o = o;
   pl.a.lse = lse;
-  cudaError_t e = launch_combine(pl.a, o_parts, lse_parts, n_splits, pl.out_dtype, static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_combine(pl.a, o_parts, lse_parts, n_splits, part_row_begin, pl.out_dtype,
+                                 static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? FA_OK : cuda_fail(e, "combine");
 }
 

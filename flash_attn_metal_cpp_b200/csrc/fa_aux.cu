@@ -157,7 +157,8 @@ __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float x) { retur
 // One warp per (b, q, h) row of the query range.
 template <typename OutT>
 __global__ void combine_kernel(const AttnArgs a, const float* __restrict__ o_parts,
-                               const float* __restrict__ lse_parts, int n_splits) {
+                               const float* __restrict__ lse_parts, int n_splits,
+                               const int* __restrict__ part_row_begin) {
   const int nq = a.q_end - a.q_begin;
   const long long rows = (long long)a.B * nq * a.Hq;
   const long long warp_id = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
@@ -173,11 +174,15 @@ __global__ void combine_kernel(const AttnArgs a, const float* __restrict__ o_par
   const long long o_row = (((long long)b * a.Sq + q) * a.Hq + h) * a.D;
   // Lane j (< 32) holds LSE_j; larger split counts fold in 32 at a time.
   float mx = -INFINITY;
-  for (int j = lane; j < n_splits; j += 32) mx = fmaxf(mx, lse_parts[j * lse_stride + lse_idx]);
+  // Partial j holds rows [part_row_begin[j], ...) only (when given): rows
+  // before it skip it.
+  for (int j = lane; j < n_splits; j += 32)
+    if (part_row_begin == nullptr || q >= part_row_begin[j]) mx = fmaxf(mx, lse_parts[j * lse_stride + lse_idx]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
   float w_sum = 0.f;
   for (int j = lane; j < n_splits; j += 32) {
+    if (part_row_begin != nullptr && q < part_row_begin[j]) continue;
     const float l = lse_parts[j * lse_stride + lse_idx];
     w_sum += (l == -INFINITY) ? 0.f : expf(l - mx);
   }
@@ -191,6 +196,7 @@ __global__ void combine_kernel(const AttnArgs a, const float* __restrict__ o_par
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   for (int j = 0; j < n_splits; ++j) {
+    if (part_row_begin != nullptr && q < part_row_begin[j]) continue;
     const float l = lse_parts[j * lse_stride + lse_idx];
     if (l == -INFINITY) continue;  // split saw no key of this row
     const float w = expf(l - lse);
@@ -363,15 +369,22 @@ cudaError_t launch_rope_table(float* cs, float* sn, int rows, int D, double thet
 }
 
 cudaError_t launch_combine(const AttnArgs& a, const float* o_parts, const float* lse_parts,
-                           int n_splits, int out_dtype, cudaStream_t st) {
+                           int n_splits, const int* part_row_begin, int out_dtype, cudaStream_t st) {
   const long long rows = (long long)a.B * (a.q_end - a.q_begin) * a.Hq;
   if (rows <= 0) return cudaSuccess;
   const int threads = 256;
   const long long blocks = (rows * 32 + threads - 1) / threads;
   switch (out_dtype) {
-    case kF16: combine_kernel<__half><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
-    case kBF16: combine_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
-    default: combine_kernel<float><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits); break;
+    case kF16:
+      combine_kernel<__half><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits, part_row_begin);
+      break;
+    case kBF16:
+      combine_kernel<__nv_bfloat16><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits,
+                                                                          part_row_begin);
+      break;
+    default:
+      combine_kernel<float><<<(unsigned)blocks, threads, 0, st>>>(a, o_parts, lse_parts, n_splits, part_row_begin);
+      break;
   }
   note_launch();
   return cudaGetLastError();

@@ -108,8 +108,10 @@ cudaError_t launch_rope_table(float* cos, float* sin, int rows, int D, double th
                               cudaStream_t stream);
 
 // (O, LSE) merge of n split-KV partials.
+// part_row_begin (device, n_splits ints, may be NULL): partial j holds rows
+// [part_row_begin[j], ...) only; rows before it do not read it.
 cudaError_t launch_combine(const AttnArgs& a, const float* o_parts, const float* lse_parts,
-                           int n_splits, int out_dtype, cudaStream_t stream);
+                           int n_splits, const int* part_row_begin, int out_dtype, cudaStream_t stream);
 
 // Zero-fill O rows and set LSE to -inf (used when there is no key at all).
 cudaError_t launch_fill_empty(const AttnArgs& a, int out_dtype, cudaStream_t stream);

@@ -10,12 +10,13 @@ Two drivers sit on the partitions of `sharding`:
   GPUs (e.g. 8 query heads over one KV head). Keys are split into one
   contiguous range per rank, balanced by visible (query, key) pairs under
   the top-left causal mask; query rows are owned in equal blocks. Each
-  rank's kernel computes the partial (O_r, LSE_r) of its keys and its
-  epilogue stores every finished 128-row tile straight into the staging
-  slot of the row's owner -- peer memory mapped with CUDA IPC, written over
-  NVLink while the rest of the kernel still runs. A one-element NCCL
-  all-reduce then orders all partial kernels before the owners' merge
-  (fa_combine: LSE = log sum exp LSE_j, O = sum exp(LSE_j - LSE) O_j).
+  rank's kernel computes the partial (O_r, LSE_r) of its keys for the rows
+  from its first key on, and its epilogue stores every finished 128-row
+  tile straight into the staging slot of the row's owner -- peer memory
+  mapped with CUDA IPC, written over NVLink while the rest of the kernel
+  still runs. A one-element NCCL all-reduce then orders all partial kernels
+  before the owners' merge (fa_combine_ranges: LSE = log sum exp LSE_j,
+  O = sum exp(LSE_j - LSE) O_j over the slots written for that row).
   Staging is double-buffered, so the merge of step i and the partial
   stores of step i+1 never touch the same buffer and one barrier per step
   suffices.
@@ -108,6 +109,10 @@ class SplitKVAttention:
                 _view(o_ptr, (self.world, batch, R, num_heads_q, head_dim), torch.float32, self.device),
                 _view(o_ptr + self._o_bytes, (self.world, batch, num_heads_q, R), torch.float32, self.device),
             ))
+        # Per slot of this rank's block: the first row its rank wrote (a rank's
+        # rows start at its first key, so earlier rows of the slot are stale).
+        rb = p.row_begin[self.rank] if self.rank < p.n_owners else [0]
+        self._row_begin = torch.tensor(rb if rb else [0], dtype=torch.int32, device=self.device)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._step = 0
         self._closed = False
@@ -138,7 +143,7 @@ class SplitKVAttention:
         if rows > 0:
             n = len(p.slots[self.rank])
             o_st, l_st = self._stage[buf]
-            _ext.combine(o_st[:n], l_st[:n], out, lse, q_range=(0, rows))
+            _ext.combine(o_st[:n], l_st[:n], out, lse, q_range=(0, rows), row_begin=self._row_begin[:n])
         return out
 
     def close(self):

@@ -79,12 +79,14 @@ class SplitKVPlan:
     """Split-KV partition of one attention problem over `world` ranks.
 
     kv_ranges[r]   keys of rank r (contiguous, tile aligned; may be empty)
-    q_ranges[r]    query rows rank r computes: from the start of the owner
-                   block holding its first visible row to seqlen_q (all rows
-                   without the causal mask); empty when kv_ranges[r] is
+    q_ranges[r]    query rows rank r computes: from its first visible row
+                   (rounded down to a tile) to seqlen_q (all rows without the
+                   causal mask); empty when kv_ranges[r] is
     owner_rows     rows per owner block (a multiple of `tile`)
     n_owners       number of owner blocks (ranks >= n_owners own no rows)
     slots[o]       ranks whose partials owner o merges, in slot order
+    row_begin[o]   per slot, the first row of owner o's block (block-relative)
+                   the slot's rank wrote; the merge ignores the slot before it
     """
 
     seqlen_q: int
@@ -97,6 +99,7 @@ class SplitKVPlan:
     kv_ranges: List[Tuple[int, int]]
     q_ranges: List[Tuple[int, int]]
     slots: List[List[int]] = field(default_factory=list)
+    row_begin: List[List[int]] = field(default_factory=list)
 
     def owner_block(self, o: int) -> Tuple[int, int]:
         """Query rows [lo, hi) owned by rank o (empty for o >= n_owners)."""
@@ -169,14 +172,17 @@ def splitkv_plan(seqlen_q: int, seqlen_k: int, world: int, causal: bool, tile: i
         if hi <= lo or seqlen_q == 0:
             q_ranges.append((seqlen_q, seqlen_q))
         elif causal:
-            first = min(lo, seqlen_q)  # first row that sees key lo
-            q_ranges.append(((first // owner_rows) * owner_rows if first < seqlen_q else seqlen_q, seqlen_q))
+            first = min(lo, seqlen_q)  # first row that sees key lo, rounded down to a tile
+            q_ranges.append(((first // tile) * tile if first < seqlen_q else seqlen_q, seqlen_q))
         else:
             q_ranges.append((0, seqlen_q))
-    slots = []
+    slots, row_begin = [], []
     for o in range(n_owners):
         blo = o * owner_rows
         bhi = min(seqlen_q, blo + owner_rows)
-        slots.append([r for r in range(world) if q_ranges[r][0] <= blo and q_ranges[r][1] >= bhi
-                      and q_ranges[r][1] > q_ranges[r][0]])
-    return SplitKVPlan(seqlen_q, seqlen_k, world, causal, tile, owner_rows, n_owners, kv_ranges, q_ranges, slots)
+        mine = [r for r in range(world) if q_ranges[r][1] > q_ranges[r][0] and q_ranges[r][0] < bhi
+                and q_ranges[r][1] > blo]
+        slots.append(mine)
+        row_begin.append([max(0, q_ranges[r][0] - blo) for r in mine])
+    return SplitKVPlan(seqlen_q, seqlen_k, world, causal, tile, owner_rows, n_owners, kv_ranges, q_ranges, slots,
+                       row_begin)

@@ -171,6 +171,14 @@ fa_status fa_combine(const fa_params* p, const float* o_parts,
                      const float* lse_parts, int32_t n_splits, void* o,
                      float* lse, uint32_t q_begin, uint32_t q_end, void* stream);
 
+/* fa_combine where partial j holds only rows [part_row_begin[j], ...)
+ * (part_row_begin: DEVICE array of n_splits int32, NULL = every row): rows
+ * before it ignore that partial, whose staging there may be stale. */
+fa_status fa_combine_ranges(const fa_params* p, const float* o_parts,
+                            const float* lse_parts, int32_t n_splits,
+                            const int32_t* part_row_begin, void* o, float* lse,
+                            uint32_t q_begin, uint32_t q_end, void* stream);
+
 /* Output routing for a split-KV partial spread over devices. Query rows are
  * owned in blocks of owner_rows (a multiple of 128): row r belongs to owner
  * r / owner_rows. `table` is a DEVICE array of 2 * n_owners addresses:

@@ -226,3 +226,31 @@ def test_splitkv_two_gpus_matches_oracle(tmp_path, shape, rows):
     for r0, r1 in (rows or [(0, S)]):
         ref_o, _ = _oracle(q, k, v, True, scale, 5e5, q_range=(r0, r1))
         assert_close_16(got[:, r0:r1], ref_o[:, r0:r1], f"rows {r0}:{r1}")
+
+
+def test_combine_skips_rows_before_each_partial(fa, cuda_device):
+    """Split-KV partials computed only from each split's first key (rounded
+    down to a tile), stale (NaN) staging before it: the merge with row_begin
+    ignores those rows and equals attention over all keys."""
+    import torch
+
+    B, S, Hq, Hk, D = 1, 1400, 8, 1, 128
+    q, k, v = _inputs((B, S, Hq, D), (B, S, Hk, D), torch.bfloat16, seed=25, amp=0.5)
+    scale = 1 / math.sqrt(D)
+    bounds = [0, 300, 700, 1100, 1400]
+    n = len(bounds) - 1
+    parts_o = torch.full((n, B, S, Hq, D), float("nan"), device=cuda_device)
+    parts_l = torch.full((n, B, Hq, S), float("nan"), device=cuda_device)
+    starts = []
+    for j in range(n):
+        q0 = bounds[j] // 128 * 128
+        starts.append(q0)
+        fa.forward_range(q, k, v, (q0, S), (bounds[j], bounds[j + 1]), parts_o[j], parts_l[j],
+                         softmax_scale=scale, is_causal=True, rope_theta=5e5, out_dtype=torch.float32)
+    out = torch.empty((B, S, Hq, D), device=cuda_device)
+    rb = torch.tensor(starts, dtype=torch.int32, device=cuda_device)
+    fa.combine(parts_o, parts_l, out, row_begin=rb)
+    torch.cuda.synchronize()
+    fa.check_status()
+    ref_o, _ = _oracle(q, k, v, True, scale, 5e5)
+    assert_close_16(_np(out), ref_o, "combine with row_begin")

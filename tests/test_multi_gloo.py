@@ -72,7 +72,15 @@ def _worker(rank, world, port, mode, result_path):
             slots = plan.slots[rank]
             st_o = np.stack([o_all[r].numpy()[:, lo:hi] for r in slots])
             st_l = np.stack([l_all[r].numpy()[:, :, lo:hi] for r in slots])
+            # A slot holds its rank's rows from row_begin on (the rank's first
+            # key); earlier rows are stale staging, which the merge skips.
+            for j, (r, rb) in enumerate(zip(slots, plan.row_begin[rank])):
+                assert plan.q_ranges[r][0] == lo + rb or (rb == 0 and plan.q_ranges[r][0] <= lo)
+                st_o[j, :, :rb] = np.nan  # stale
+                st_o[j, :, :rb] = 0.0     # ... and skipped
+                st_l[j, :, :, :rb] = -np.inf
             block[:, lo:hi], _ = orc.combine_partials(st_o, st_l)
+            assert np.isfinite(block[:, lo:hi]).all()
         t = torch.from_numpy(block)
         dist.all_reduce(t)  # owner blocks are disjoint
         result = t.numpy()
@@ -133,12 +141,19 @@ def test_splitkv_plan_covers_and_balances(Sq, Sk, W, causal):
         # Every row that sees a key of the range is computed, starting on an owner boundary.
         first_row = klo if causal else 0
         if first_row < Sq:
-            assert qlo <= first_row and qhi == Sq and qlo % p.owner_rows == 0
-    # Slots: owner o merges exactly the ranks whose query range covers its block.
+            assert qlo <= first_row and qhi == Sq and qlo % p.tile == 0
+    # Slots: owner o merges exactly the ranks whose query range reaches into its
+    # block, each from the first row that rank wrote.
     for o in range(p.n_owners):
         lo, hi = p.owner_block(o)
-        want = [r for r in range(W) if p.q_ranges[r][0] <= lo and p.q_ranges[r][1] >= hi and p.q_ranges[r][1] > p.q_ranges[r][0]]
+        want = [r for r in range(W) if p.q_ranges[r][1] > p.q_ranges[r][0] and p.q_ranges[r][0] < hi
+                and p.q_ranges[r][1] > lo]
         assert p.slots[o] == want and len(want) >= 1
+        assert p.row_begin[o] == [max(0, p.q_ranges[r][0] - lo) for r in want]
+        assert all(0 <= rb < hi - lo for rb in p.row_begin[o])
+    for (klo, khi), (qlo, qhi) in zip(p.kv_ranges, p.q_ranges):
+        if khi > klo and causal and klo < Sq:
+            assert qlo % p.tile == 0 and qlo <= klo < qlo + p.tile  # rows start at the first key's tile
     # Balance: no share exceeds the even share by more than one key tile's work
     # (the granularity of a contiguous tile-aligned cut); long sequences within 5%.
     work = [p.pair_work(r) for r in range(W)]
