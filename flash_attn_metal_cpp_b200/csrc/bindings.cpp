@@ -332,7 +332,7 @@ void py_forward_range(py::object Q, py::object K, py::object V, std::pair<int64_
                       std::pair<int64_t, int64_t> kv_range, py::object out, py::object lse,
                       float softmax_scale, bool is_causal, py::object cos, py::object sin,
                       py::object rope_theta, py::object out_dtype, py::object route, int n_owners,
-                      int64_t owner_rows) {
+                      int64_t owner_rows, py::object window_size, py::object alibi_slopes) {
   require_cuda(Q, "Q");
   require_cuda(K, "K");
   require_cuda(V, "V");
@@ -345,8 +345,16 @@ void py_forward_range(py::object Q, py::object K, py::object V, std::pair<int64_
   const bool rotary_tables = !cos.is_none() && !sin.is_none();
   const float theta = rope_theta.is_none() ? 0.f : rope_theta.cast<float>();
   fa_params p;
-  fill_params(p, qs, ks, softmax_scale, is_causal, 0.f, py::none(), py::none(), rotary_tables || theta > 0.f,
+  fill_params(p, qs, ks, softmax_scale, is_causal, 0.f, alibi_slopes, window_size, rotary_tables || theta > 0.f,
               theta);
+  py::object slopes = py::none();
+  if (!alibi_slopes.is_none()) {
+    py::module_ torch = py::module_::import("torch");
+    slopes = torch.attr("as_tensor")(alibi_slopes, py::arg("dtype") = torch.attr("float32"),
+                                     py::arg("device") = Q.attr("device")).attr("contiguous")();
+    check_slopes(slopes.attr("numel")().cast<int64_t>(), qs[2]);
+    p.alibi_slopes = tptr<const float>(slopes);
+  }
   p.dtype = code;
   p.out_dtype = parse_out_dtype(out_dtype);
   const int oc = p.out_dtype < 0 ? code : p.out_dtype;
@@ -594,6 +602,7 @@ PYBIND11_MODULE(_flash_attn_metal, m) {
         py::arg("softmax_scale") = 0.0f, py::arg("is_causal") = false, py::arg("cos") = py::none(),
         py::arg("sin") = py::none(), py::arg("rope_theta") = py::none(), py::arg("out_dtype") = py::none(),
         py::arg("route") = py::none(), py::arg("n_owners") = 0, py::arg("owner_rows") = 0,
+        py::arg("window_size") = py::none(), py::arg("alibi_slopes") = py::none(),
         "Rows q_range of the attention over keys kv_range (CUDA tensors, current stream)");
   m.def("combine", &py_combine, py::arg("o_parts"), py::arg("lse_parts"), py::arg("out"),
         py::arg("lse") = py::none(), py::arg("q_range") = py::none(), py::arg("row_begin") = py::none(),

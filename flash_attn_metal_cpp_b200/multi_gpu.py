@@ -120,7 +120,8 @@ class SplitKVAttention:
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float,
                 cos=None, sin=None, rope_theta: Optional[float] = None, out: Optional[torch.Tensor] = None,
-                lse: Optional[torch.Tensor] = None, out_dtype=None) -> torch.Tensor:
+                lse: Optional[torch.Tensor] = None, out_dtype=None, window_size=None,
+                alibi_slopes=None) -> torch.Tensor:
         if self._closed:
             raise RuntimeError("SplitKVAttention is closed")
         p = self.plan
@@ -132,7 +133,7 @@ class SplitKVAttention:
             _ext.forward_range(q, k, v, (qlo, qhi), (klo, khi), softmax_scale=softmax_scale,
                                is_causal=self.causal, cos=cos, sin=sin, rope_theta=rope_theta,
                                out_dtype=torch.float32, route=self._routes[buf], n_owners=p.n_owners,
-                               owner_rows=p.owner_rows)
+                               owner_rows=p.owner_rows, window_size=window_size, alibi_slopes=alibi_slopes)
         # Every partial kernel precedes every owner's merge (stream-ordered).
         dist.all_reduce(self._flag, group=self.group)
         lo, hi = p.owner_block(self.rank)
@@ -176,9 +177,11 @@ class QShardAttention:
         self._side = torch.cuda.Stream(self.device)
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float, causal: bool,
-                out: torch.Tensor, cos=None, sin=None, rope_theta: Optional[float] = None) -> torch.Tensor:
+                out: torch.Tensor, cos=None, sin=None, rope_theta: Optional[float] = None, window_size=None,
+                alibi_slopes=None) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
-        kw = dict(softmax_scale=softmax_scale, is_causal=causal, cos=cos, sin=sin, rope_theta=rope_theta)
+        kw = dict(softmax_scale=softmax_scale, is_causal=causal, cos=cos, sin=sin, rope_theta=rope_theta,
+                  window_size=window_size, alibi_slopes=alibi_slopes)
         Sk = k.shape[1]
         self._side.wait_stream(main)  # inputs written on the main stream are ready
         for i, (lo, hi) in enumerate(self.ranges):

@@ -254,3 +254,23 @@ def test_combine_skips_rows_before_each_partial(fa, cuda_device):
     fa.check_status()
     ref_o, _ = _oracle(q, k, v, True, scale, 5e5)
     assert_close_16(_np(out), ref_o, "combine with row_begin")
+
+
+def test_forward_range_with_window_and_alibi(fa, cuda_device):
+    """forward_range takes the same window / ALiBi arguments as forward: a
+    partial over a key range with both matches the oracle."""
+    import torch
+
+    B, S, Hq, Hk, D = 1, 900, 4, 2, 128
+    q, k, v = _inputs((B, S, Hq, D), (B, S, Hk, D), torch.float16, seed=26)
+    scale = 1 / math.sqrt(D)
+    sl = np.array([0.5, 0.25, 0.125, 0.0625], np.float32)
+    out = torch.full((B, S, Hq, D), float("nan"), device=cuda_device)
+    lse = torch.full((B, Hq, S), float("nan"), device=cuda_device)
+    fa.forward_range(q, k, v, (128, 900), (200, 800), out, lse, softmax_scale=scale, is_causal=True,
+                     out_dtype=torch.float32, window_size=(300, -1), alibi_slopes=torch.from_numpy(sl))
+    torch.cuda.synchronize()
+    fa.check_status()
+    ref_o, ref_l = _oracle(q, k, v, True, scale, None, q_range=(128, 900), kv_range=(200, 800), window=(300, -1),
+                           alibi_slopes=sl)
+    _check_rows(_np(out), _np(lse), ref_o, ref_l, (128, 900), False, "forward_range window+alibi")
