@@ -54,7 +54,12 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsOther <= kThreads * kRegsLaunc
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;  // + t * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
-constexpr int kPolyPairs = 4;  // of every 16 exp2 pairs, this many run as a polynomial on the FMA pipe
+// Of every 16 exp2 pairs, this many run as a polynomial on the FMA pipe
+// (exp2_poly2) instead of MUFU ex2. Measured on this kernel (cfg4 / cfg5a
+// kernel TFLOP/s): 0 -> 1078 / 1075, 2 -> 1063 / 1055, 4 -> 1051 / 1036,
+// 6 -> 1032 / 1010; the extra FMA-pipe instructions cost more issue slots
+// (and power, under the power cap) than the MUFU time they save.
+constexpr int kPolyPairs = 0;
 
 template <int D>
 struct Cfg {
