@@ -97,7 +97,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
@@ -118,24 +118,28 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
-        sm, mx, reasons = [], [], set()
+        rows, reasons = [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3])))
             except ValueError:
                 continue
             for n, v in zip(names, parts[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        if not sm:
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        # "Under load": samples drawing at least 60 % of the highest power seen
+        # (the sampler also runs a little before and after the timed region).
+        p_max = max(r[2] for r in rows)
+        loaded = [r for r in rows if r[2] >= 0.6 * p_max] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded),
+                "power_w_max": p_max}
 
 
 def make_inputs(cfg, device, seed):
@@ -214,8 +218,8 @@ def run_reference(args, cfg, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg4")
     ap.add_argument("--e2e-steps", type=int, default=5)
@@ -297,7 +301,10 @@ def main():
     props = torch.cuda.get_device_properties(device)
     sampler = ClockSampler(f"GPU-{props.uuid}" if getattr(props, "uuid", None) else str(local_rank))
     stream = torch.cuda.current_stream(device)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # One event per step boundary: the first and last bracket the timed
+    # region, the ones between give per-step times (median / p10 / p90).
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    ev0, ev1 = evs[0], evs[-1]
     sampler.start()
     time.sleep(0.3)
     n_launch0 = fa.launch_count()
@@ -306,9 +313,9 @@ def main():
         dist.barrier()
     torch.cuda.synchronize()
     ev0.record(stream)
-    for _ in range(args.steps):
+    for i in range(args.steps):
         step()
-    ev1.record(stream)
+        evs[i + 1].record(stream)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -317,6 +324,10 @@ def main():
     clocks = sampler.stop()
     fa.check_status()
     elapsed_ms = ev0.elapsed_time(ev1)
+    step_ms = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps))
+
+    def pct(p_):
+        return step_ms[min(len(step_ms) - 1, int(round(p_ * (len(step_ms) - 1))))]
     t = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -392,6 +403,7 @@ def main():
                "h2d_bytes_per_step": int(h2d[0].item()), "d2h_bytes_per_step": int(h2d[1].item())}
 
     peaks, peak_kind = load_peaks()
+    alg_bytes = sum(x.numel() * x.element_size() for x in (q, k, v, out)) * (share if shared else 1.0)
     kern_avg_ms = kern_ms / max(kern_launches, 1)
     if shared and not split_kv:
         # Two concurrent launches per step: time the pair by the step itself.
@@ -445,6 +457,13 @@ def main():
             "pct_of_peak": {"measured_" + ("sustained" if long_region else "burst"): value / world / peak,
                             "datasheet_2250": value / world / DATASHEET_BF16_TFLOPS},
             "roofline": roofline,
+            "step_ms_rank0": {"median": pct(0.5), "p10": pct(0.1), "p90": pct(0.9), "n": len(step_ms)},
+            # Memory-side sanity check: algorithmic bytes (Q, K, V read once, O
+            # written once, as the caller holds them) over the step time.
+            "hbm": {"algorithmic_bytes_per_step_per_gpu": alg_bytes,
+                    "achieved_gbs": alg_bytes / (ms_per_step / 1e3) / 1e9,
+                    "peak_gbs": peaks["hbm_gbs"],
+                    "frac": alg_bytes / (ms_per_step / 1e3) / 1e9 / peaks["hbm_gbs"]},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": gpu_launches,
