@@ -424,12 +424,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
       const float2 sc2 = make_float2(sl2, sl2), nm2 = make_float2(-m_sub, -m_sub);
 #pragma unroll
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t p[16];
+      // Two halves of 64 keys with one 32-column P store each: 1-1.5 % faster
+      // than four 16-column stores (fewer asynchronous stores whose source
+      // registers the next chunk's results would have to wait for).
+      for (int h = 0; h < 2; ++h) {
+        uint32_t p[32];
         if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int c = c0 + 2 * i;
+          for (int i = 0; i < 32; ++i) {
+            const int c = h * 64 + 2 * i;
             const float p0 = (c < key_lim && c >= key_beg) ? ex2_approx(fmaf(s[c], sl2, -m_sub)) : 0.f;
             const float p1 = (c + 1 < key_lim && c + 1 >= key_beg) ? ex2_approx(fmaf(s[c + 1], sl2, -m_sub)) : 0.f;
             acc0 = __fadd2_rn(acc0, make_float2(p0, p1));
@@ -437,18 +440,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int c = c0 + 2 * i;
+          for (int i = 0; i < 32; ++i) {
+            const int c = h * 64 + 2 * i;
             const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sc2, nm2);
-            // kPolyPairs of every 16 pairs go to the FMA pipe, the rest to MUFU.
-            const float2 e = (i < kPolyPairs) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            const float2 e = ((i & 15) < kPolyPairs) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
             if (i & 1) acc1 = __fadd2_rn(acc1, e);
             else acc0 = __fadd2_rn(acc0, e);
             p[i] = pack_half2(e.x, e.y);
           }
         }
-        tmem_st16(tS + c0 / 2, p);  // P columns [c0/2, c0/2+16) of S_t's region
-        if (c0 == 32) {  // keys [0, 64) done: let the first half of PV start
+        tmem_st32(tS + h * 32, p);  // P columns [32h, 32h+32) of S_t's region
+        if (h == 0) {  // keys [0, 64) done: let the first half of PV start
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
