@@ -592,6 +592,11 @@ PYBIND11_MODULE(_flash_attn_metal, m) {
     if (st != FA_OK) throw std::runtime_error(err_text(st));
     return py::make_tuple(ms, n);
   }, "(summed ms, launches) of the attention kernel since kernel_timing_enable; disables timing");
+  m.def("set_wait_limit", [](double seconds) {
+    fa_status st = fa_set_wait_limit(seconds);
+    if (st != FA_OK) throw std::runtime_error(err_text(st));
+  }, py::arg("seconds"), "Wall-clock limit of every in-kernel wait of later launches (default 2 s)");
+  m.def("get_wait_limit", []() { return fa_get_wait_limit(); }, "Current in-kernel wait limit in seconds");
   m.def("pool_stats", &py_pool_stats, "(hits, misses, bytes reserved) of the device buffer pool");
   m.def("pool_clear", []() {
     fa_status st = fa_pool_clear();

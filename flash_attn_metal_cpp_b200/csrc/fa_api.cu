@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -33,6 +34,11 @@ namespace {
 
 thread_local std::string g_last_error;
 thread_local uint64_t g_launches = 0;
+// Limit of every in-kernel wait (fa_set_wait_limit; 0 = the kernels' default).
+std::atomic<unsigned long long> g_wait_limit_ns{0};
+// Test hook (fa_test_stall_next_launch): K tile to withhold in the next
+// tensor-core launch of this thread (0 = none).
+thread_local int g_stall_k_tile = 0;
 // Attention-kernel timing (fa_kernel_timing_enable / _read).
 thread_local bool g_timing = false;
 thread_local std::vector<std::pair<cudaEvent_t, cudaEvent_t>> g_events;
@@ -139,15 +145,19 @@ struct DeviceState {
   cudaStream_t d2h_stream = nullptr;    // host-pointer path: copies out
   DevicePool pool;
   std::mutex mu;                    // serialises the host-pointer path and the caches
-  // RoPE table cache: (theta bits, D) -> tables with `rows` rows.
+  // RoPE table cache: (theta, D) -> tables with `rows` rows (grown on demand).
   struct Rope {
-    float theta = 0.f;
-    int D = 0, rows = 0;
+    int rows = 0;
     float* cs = nullptr;
     float* sn = nullptr;
-  } rope;
+  };
+  std::map<std::pair<float, int>, Rope> rope;
   // Stream-ordered workspaces for fa_forward calls without a workspace.
   std::map<cudaStream_t, std::pair<void*, size_t>> ws;
+  // Buffers replaced by larger ones. Another host thread may still hold (and
+  // be about to enqueue work on) a replaced pointer, so none is freed before
+  // fa_pool_clear, which synchronises the device first.
+  std::vector<void*> retired;
 };
 
 std::mutex g_devices_mu;
@@ -303,6 +313,8 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
   pl->need_q16 = pl->tc && pl->rope;
   pl->need_k16 = pl->tc && pl->rope;
   pl->need_v16 = pl->tc && p->dtype == kBF16;
+  // Workspace: the staging pass's range record (kRangeRecBytes), then the
+  // staged fp16 operands (and, for padded head dims, the padded output).
   size_t ws = 0;
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
   if (pl->need_q16) ws += up((size_t)a.B * a.Sq * a.Hq * D * 2);
@@ -313,7 +325,7 @@ fa_status make_plan(const fa_params* p, Plan* pl) {
     ws = up((size_t)a.B * a.Sq * a.Hq * dp * 2) + 2 * up((size_t)a.B * a.Sk * a.Hk * dp * 2) +
          up((size_t)a.B * a.Sq * a.Hq * dp * dtype_size(out_dt));
   }
-  pl->ws_bytes = ws;
+  pl->ws_bytes = ws ? ws + kRangeRecBytes : 0;
   return FA_OK;
 }
 
@@ -335,24 +347,42 @@ fa_status encode_map(CUtensorMap* m, const void* base, bool bf16, int D, int H, 
   return FA_OK;
 }
 
-// Cached RoPE tables from theta with at least `rows` rows.
+// Cached RoPE tables from theta with at least `rows` rows, one entry per
+// (theta, D). A table that grows is replaced by a new allocation; the old
+// one is retired (freed only by fa_pool_clear), since a call on another
+// stream or thread may still read it. The new tables are built on `stream`;
+// a call on another stream that then finds them waits for that build
+// through `ready`.
 fa_status rope_from_theta(DeviceState* ds, float theta, int D, int rows, cudaStream_t stream,
                           const float** cs, const float** sn) {
   std::lock_guard<std::mutex> g(ds->mu);
-  auto& r = ds->rope;
-  if (!(r.cs && r.theta == theta && r.D == D && r.rows >= rows)) {
+  auto& r = ds->rope[std::make_pair(theta, D)];
+  if (!(r.cs && r.rows >= rows)) {
     if (r.cs) {
-      FA_CUDA(cudaStreamSynchronize(stream));
-      cudaFree(r.cs);
-      cudaFree(r.sn);
+      ds->retired.push_back(r.cs);
+      ds->retired.push_back(r.sn);
       r.cs = r.sn = nullptr;
+      r.rows = 0;
     }
     const size_t bytes = (size_t)rows * (D / 2) * sizeof(float) + 16;
-    FA_CUDA(cudaMalloc(&r.cs, bytes));
-    FA_CUDA(cudaMalloc(&r.sn, bytes));
-    FA_CUDA(launch_rope_table(r.cs, r.sn, rows, D, (double)theta, stream));
-    r.theta = theta;
-    r.D = D;
+    float *c = nullptr, *s = nullptr;
+    FA_CUDA(cudaMalloc(&c, bytes));
+    cudaError_t e = cudaMalloc(&s, bytes);
+    if (e != cudaSuccess) {
+      cudaFree(c);
+      return cuda_fail(e, "cudaMalloc (RoPE tables)");
+    }
+    e = launch_rope_table(c, s, rows, D, (double)theta, stream);
+    // Other streams must not read the tables before they are built: finish
+    // the build here (once per (theta, D) and size, outside any hot loop).
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      cudaFree(c);
+      cudaFree(s);
+      return cuda_fail(e, "RoPE tables");
+    }
+    r.cs = c;
+    r.sn = s;
     r.rows = rows;
   }
   *cs = r.cs;
@@ -360,29 +390,65 @@ fa_status rope_from_theta(DeviceState* ds, float theta, int D, int rows, cudaStr
   return FA_OK;
 }
 
+// Per-stream workspace, grown on demand. A replaced buffer is retired, not
+// freed: another host thread may hold it for a call it is still enqueuing
+// on the same stream.
 fa_status stream_workspace(DeviceState* ds, cudaStream_t stream, size_t bytes, void** out) {
   std::lock_guard<std::mutex> g(ds->mu);
   auto& w = ds->ws[stream];
   if (w.second < bytes) {
-    if (w.first) {
-      FA_CUDA(cudaStreamSynchronize(stream));
-      cudaFree(w.first);
-      w.first = nullptr;
-      w.second = 0;
-    }
+    if (w.first) ds->retired.push_back(w.first);
+    w.first = nullptr;
+    w.second = 0;
     FA_CUDA(cudaMalloc(&w.first, bytes));
     w.second = bytes;
+    // The staging record must start at zero; the staging kernels keep it so.
+    FA_CUDA(cudaMemsetAsync(w.first, 0, kRangeRecBytes, stream));
   }
   *out = w.first;
   return FA_OK;
 }
 
+// Job staging rows [lo, hi) of one (B, S, H, D) tensor into the fp16
+// buffer y ([B, S, H, Dp] contiguous) at the same rows.
+StageJob stage_job(const void* x, int dtype, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H, int D,
+                   int Dp, int lo, int hi, const float* cs, const float* sn, __half* y, int slot) {
+  StageJob j;
+  const int hd = D / 2;
+  j.x = static_cast<const uint8_t*>(x) + (size_t)lo * ss * dtype_size(dtype);
+  j.sb = sb;
+  j.ss = ss;
+  j.sh = sh;
+  j.B = B;
+  j.S = hi - lo;
+  j.H = H;
+  j.D = D;
+  j.Dp = Dp;
+  j.cs = cs ? cs + (size_t)lo * hd : nullptr;
+  j.sn = sn ? sn + (size_t)lo * hd : nullptr;
+  j.y = y + (size_t)lo * H * Dp;
+  j.y_rows = S;
+  j.slot = slot;
+  return j;
+}
+
 // Core of fa_forward / fa_forward_partial once the plan is fixed.
+// Core of every forward entry point once the plan is fixed. `ds` supplies
+// the cached RoPE tables and per-stream workspace; it may be NULL when the
+// caller passes both (cos/sin when RoPE is on, and a workspace when
+// pl.ws_bytes > 0), which is how the allocation-free entry point calls it.
 fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float* cos,
               const float* sin, void* workspace, size_t ws_bytes, cudaStream_t stream,
-              DeviceState* ds) {
+              DeviceState* ds, unsigned* status) {
   AttnArgs& a = pl.a;
-  a.status = ds->status;
+  a.status = status;
+  a.wait_limit_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  a.skip_k_tile = 0;
+  a.range_exp = nullptr;
+  // A workspace from the caller (or the host path's pool) may hold anything:
+  // clear its staging record. The per-stream workspace is cleared once when
+  // allocated and kept clear by the staging kernels.
+  const bool clear_record = workspace != nullptr && pl.ws_bytes > 0;
   if (a.q_end <= a.q_begin || a.B == 0 || a.Hq == 0) return FA_OK;
   if (!a.o && a.route_rows == 0) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
   // No key at all (Sk == 0 or an empty split): O = 0, LSE = -inf.
@@ -397,6 +463,7 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     if (!(pl.rope_theta > 0.f) || !std::isfinite(pl.rope_theta))
       return fail(FA_ERR_INVALID_ARG, "has_rotary needs cos/sin tables or rope_theta > 0");
     if (a.D % 2 != 0) return fail(FA_ERR_UNSUPPORTED, "RoPE from rope_theta needs an even head_dim");
+    if (ds == nullptr) return fail(FA_ERR_INVALID_ARG, "RoPE tables missing");
     fa_status st = rope_from_theta(ds, pl.rope_theta, a.D, a.Sq > a.Sk ? a.Sq : a.Sk, stream, &cs, &sn);
     if (st != FA_OK) return st;
   }
@@ -408,13 +475,16 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     // workspace, and its first D columns are copied to the caller's O.
     if (a.route_rows > 0) return fail(FA_ERR_UNSUPPORTED, "routed output needs head_dim 64 or 128");
     if (workspace == nullptr) {
+      if (ds == nullptr) return fail(FA_ERR_INVALID_ARG, "workspace missing");
       fa_status st = stream_workspace(ds, stream, pl.ws_bytes, &workspace);
       if (st != FA_OK) return st;
     } else if (ws_bytes < pl.ws_bytes) {
       return fail(FA_ERR_INVALID_ARG, "workspace smaller than fa_workspace_size()");
     }
     const int Dp = pl.d_pad;
-    uint8_t* wp = static_cast<uint8_t*>(workspace);
+    RangeRec* rec = static_cast<RangeRec*>(workspace);
+    if (clear_record) FA_CUDA(cudaMemsetAsync(rec, 0, kRangeRecBytes, stream));
+    uint8_t* wp = static_cast<uint8_t*>(workspace) + kRangeRecBytes;
     auto take = [&](size_t bytes) {
       uint8_t* r = wp;
       wp += (bytes + 255) & ~size_t(255);
@@ -424,24 +494,19 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     __half* k16 = reinterpret_cast<__half*>(take((size_t)a.B * a.Sk * a.Hk * Dp * 2));
     __half* v16 = reinterpret_cast<__half*>(take((size_t)a.B * a.Sk * a.Hk * Dp * 2));
     void* opad = take((size_t)a.B * a.Sq * a.Hq * Dp * dtype_size(pl.out_dtype));
-    const size_t esz = dtype_size(pl.dtype);
     const int q_lo = a.q_begin, q_hi = std::min(a.Sq, a.q_begin + (a.q_end - a.q_begin + 127) / 128 * 128);
     const int k_lo = a.kv_begin, k_hi = std::min(a.Sk, a.kv_begin + (a.kv_end - a.kv_begin + 127) / 128 * 128);
-    const int hd = a.D / 2;
-    cudaError_t e = launch_prep_pad(static_cast<const uint8_t*>(q) + (size_t)q_lo * a.q_ss * esz, pl.dtype, a.q_sb,
-                                    a.q_ss, a.q_sh, a.B, q_hi - q_lo, a.Hq, a.D, Dp,
-                                    cs ? cs + (size_t)q_lo * hd : nullptr, sn ? sn + (size_t)q_lo * hd : nullptr,
-                                    q16 + (size_t)q_lo * a.Hq * Dp, a.Sq, ds->status, stream);
-    if (e == cudaSuccess)
-      e = launch_prep_pad(static_cast<const uint8_t*>(k) + (size_t)k_lo * a.k_ss * esz, pl.dtype, a.k_sb, a.k_ss,
-                          a.k_sh, a.B, k_hi - k_lo, a.Hk, a.D, Dp, cs ? cs + (size_t)k_lo * hd : nullptr,
-                          sn ? sn + (size_t)k_lo * hd : nullptr, k16 + (size_t)k_lo * a.Hk * Dp, a.Sk, ds->status,
-                          stream);
-    if (e == cudaSuccess)
-      e = launch_prep_pad(static_cast<const uint8_t*>(v) + (size_t)k_lo * a.v_ss * esz, pl.dtype, a.v_sb, a.v_ss,
-                          a.v_sh, a.B, k_hi - k_lo, a.Hk, a.D, Dp, nullptr, nullptr,
-                          v16 + (size_t)k_lo * a.Hk * Dp, a.Sk, ds->status, stream);
+    StageBatch sb{};
+    sb.in_dtype = pl.dtype;
+    sb.rec = rec;
+    sb.job[0] = stage_job(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, Dp, q_lo, q_hi, cs, sn, q16, 0);
+    sb.job[1] = stage_job(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, Dp, k_lo, k_hi, cs, sn, k16, 1);
+    sb.job[2] = stage_job(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, Dp, k_lo, k_hi, nullptr,
+                          nullptr, v16, 2);
+    sb.n = 3;
+    cudaError_t e = launch_stage(sb, stream);
     if (e != cudaSuccess) return cuda_fail(e, "padded staging");
+    a.range_exp = rec->exp;
     AttnArgs ap = a;
     ap.D = Dp;
     ap.o = opad;
@@ -462,6 +527,8 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
       FA_CUDA(cudaEventCreate(&ev1));
       FA_CUDA(cudaEventRecord(ev0, stream));
     }
+    ap.skip_k_tile = g_stall_k_tile;
+    g_stall_k_tile = 0;
     e = launch_attn_sm100(ap, tq, tk, tv, false, pl.out_dtype, stream);
     if (g_timing) {
       FA_CUDA(cudaEventRecord(ev1, stream));
@@ -498,6 +565,7 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     return fail(FA_ERR_INVALID_ARG, "tensor base addresses must be 16-byte aligned");
   if (pl.ws_bytes > 0) {
     if (workspace == nullptr) {
+      if (ds == nullptr) return fail(FA_ERR_INVALID_ARG, "workspace missing");
       fa_status st = stream_workspace(ds, stream, pl.ws_bytes, &workspace);
       if (st != FA_OK) return st;
     } else if (ws_bytes < pl.ws_bytes) {
@@ -506,12 +574,7 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
       return fail(FA_ERR_INVALID_ARG, "workspace must be 16-byte aligned");
     }
   }
-  uint8_t* wp = static_cast<uint8_t*>(workspace);
-  auto take = [&](size_t bytes) {
-    uint8_t* r = wp;
-    wp += (bytes + 255) & ~size_t(255);
-    return reinterpret_cast<__half*>(r);
-  };
+  cudaError_t e;
   const void* qs = q;
   const void* ks = k;
   const void* vs = v;
@@ -519,42 +582,49 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
   int64_t k_sb = a.k_sb, k_ss = a.k_ss, k_sh = a.k_sh;
   int64_t v_sb = a.v_sb, v_ss = a.v_ss, v_sh = a.v_sh;
   bool qk_bf16 = (pl.dtype == kBF16);
-  cudaError_t e;
-  // Only the rows the kernel's tiles can load are staged: the query range and
-  // the key range, each rounded up to whole 128-row tiles.
-  const size_t esz = dtype_size(pl.dtype);
-  const int q_lo = a.q_begin, q_hi = std::min(a.Sq, a.q_begin + (a.q_end - a.q_begin + 127) / 128 * 128);
-  const int k_lo = a.kv_begin, k_hi = std::min(a.Sk, a.kv_begin + (a.kv_end - a.kv_begin + 127) / 128 * 128);
-  const int hd = a.D / 2;
-  if (pl.need_q16) {
-    __half* y = take((size_t)a.B * a.Sq * a.Hq * a.D * 2);
-    e = launch_prep_fp16(static_cast<const uint8_t*>(q) + (size_t)q_lo * a.q_ss * esz, pl.dtype, a.q_sb,
-                         a.q_ss, a.q_sh, a.B, q_hi - q_lo, a.Hq, a.D, cs ? cs + (size_t)q_lo * hd : nullptr,
-                         sn ? sn + (size_t)q_lo * hd : nullptr, y + (size_t)q_lo * a.Hq * a.D,
-                         a.Sq, ds->status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep Q");
-    qs = y;
-    q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
-  }
-  if (pl.need_k16) {
-    __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(static_cast<const uint8_t*>(k) + (size_t)k_lo * a.k_ss * esz, pl.dtype, a.k_sb,
-                         a.k_ss, a.k_sh, a.B, k_hi - k_lo, a.Hk, a.D, cs ? cs + (size_t)k_lo * hd : nullptr,
-                         sn ? sn + (size_t)k_lo * hd : nullptr, y + (size_t)k_lo * a.Hk * a.D,
-                         a.Sk, ds->status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep K");
-    ks = y;
-    k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
-  }
-  if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
-  if (pl.need_v16) {
-    __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(static_cast<const uint8_t*>(v) + (size_t)k_lo * a.v_ss * esz, pl.dtype, a.v_sb,
-                         a.v_ss, a.v_sh, a.B, k_hi - k_lo, a.Hk, a.D, nullptr, nullptr,
-                         y + (size_t)k_lo * a.Hk * a.D, a.Sk, ds->status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep V");
-    vs = y;
-    v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
+  if (pl.ws_bytes > 0) {
+    // One staging launch for every operand that needs it (RoPE and / or
+    // fp16), then the range fixup. Only the rows the kernel's tiles can load
+    // are staged: the query range and the key range, each rounded up to
+    // whole 128-row tiles.
+    RangeRec* rec = static_cast<RangeRec*>(workspace);
+    if (clear_record) FA_CUDA(cudaMemsetAsync(rec, 0, kRangeRecBytes, stream));
+    uint8_t* wp = static_cast<uint8_t*>(workspace) + kRangeRecBytes;
+    auto take = [&](size_t bytes) {
+      uint8_t* r = wp;
+      wp += (bytes + 255) & ~size_t(255);
+      return reinterpret_cast<__half*>(r);
+    };
+    const int q_lo = a.q_begin, q_hi = std::min(a.Sq, a.q_begin + (a.q_end - a.q_begin + 127) / 128 * 128);
+    const int k_lo = a.kv_begin, k_hi = std::min(a.Sk, a.kv_begin + (a.kv_end - a.kv_begin + 127) / 128 * 128);
+    StageBatch sb{};
+    sb.in_dtype = pl.dtype;
+    sb.rec = rec;
+    if (pl.need_q16) {
+      __half* y = take((size_t)a.B * a.Sq * a.Hq * a.D * 2);
+      sb.job[sb.n++] = stage_job(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, a.D, q_lo, q_hi, cs, sn,
+                                 y, 0);
+      qs = y;
+      q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
+    }
+    if (pl.need_k16) {
+      __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+      sb.job[sb.n++] = stage_job(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, a.D, k_lo, k_hi, cs, sn,
+                                 y, 1);
+      ks = y;
+      k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
+    }
+    if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
+    if (pl.need_v16) {
+      __half* y = take((size_t)a.B * a.Sk * a.Hk * a.D * 2);
+      sb.job[sb.n++] = stage_job(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, a.D, k_lo, k_hi,
+                                 nullptr, nullptr, y, 2);
+      vs = y;
+      v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
+    }
+    e = launch_stage(sb, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "fp16 staging");
+    a.range_exp = rec->exp;
   }
   CUtensorMap tq, tk, tv;
   fa_status st = encode_map(&tq, qs, qk_bf16, a.D, a.Hq, a.Sq, a.B, q_sb, q_ss, q_sh);
@@ -570,6 +640,8 @@ fa_status run(Plan& pl, const void* q, const void* k, const void* v, const float
     FA_CUDA(cudaEventCreate(&ev1));
     FA_CUDA(cudaEventRecord(ev0, stream));
   }
+  a.skip_k_tile = g_stall_k_tile;
+  g_stall_k_tile = 0;
   e = launch_attn_sm100(a, tq, tk, tv, qk_bf16, pl.out_dtype, stream);
   if (g_timing) {
     FA_CUDA(cudaEventRecord(ev1, stream));
@@ -656,7 +728,7 @@ fa_status fa_forward(const fa_params* p, const void* q, const void* k, const voi
   if (st != FA_OK) return st;
   pl.a.o = o;
   pl.a.lse = lse;
-  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds, ds->status);
 }
 
 fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k, const void* v,
@@ -682,7 +754,7 @@ fa_status fa_forward_partial(const fa_params* p, const void* q, const void* k, c
   pl.a.kv_end = (int)kv_end;
   pl.a.o = o_partial;
   pl.a.lse = lse_partial;
-  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds, ds->status);
 }
 
 fa_status fa_combine(const fa_params* p, const float* o_parts, const float* lse_parts, int32_t n_splits,
@@ -745,7 +817,7 @@ fa_status fa_forward_range(const fa_params* p, const void* q, const void* k, con
   a.kv_end = (int)kv_end;
   a.o = o;
   a.lse = lse;
-  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds);
+  return run(pl, q, k, v, cos, sin, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), ds, ds->status);
 }
 
 // ------------------------------------------------------------ CUDA IPC
@@ -868,7 +940,7 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
     pl.a.o = dout.p;
     pl.a.lse = static_cast<float*>(dl.p);
     st = run(pl, dq.p ? dq.p : (const void*)1, dk.p ? dk.p : (const void*)1, dv.p ? dv.p : (const void*)1, tc,
-             tsn, dws.p, pl.ws_bytes, s, ds);
+             tsn, dws.p, pl.ws_bytes, s, ds, ds->status);
     if (st != FA_OK) {
       cudaStreamSynchronize(s);
       return st;
@@ -936,7 +1008,7 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
     sub.a.lse = dl.p ? static_cast<float*>(dl.p) + (size_t)ch.b * a.Hq * a.Sq : nullptr;
     st = run(sub, static_cast<const char*>(dq.p) + (size_t)ch.b * a.Sq * q_row * in_sz,
              static_cast<const char*>(dk.p) + k_off * in_sz, static_cast<const char*>(dv.p) + k_off * in_sz, tc, tsn,
-             dws.p, pl.ws_bytes, s, ds);
+             dws.p, pl.ws_bytes, s, ds, ds->status);
     if (st != FA_OK) break;
     e = cudaEventRecord(ev_done[c], s);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev_done[c], 0);
@@ -989,6 +1061,17 @@ fa_status fa_pool_clear(void) {
   if (st != FA_OK) return st;
   FA_CUDA(cudaDeviceSynchronize());
   ds->pool.clear();
+  // With the device idle no call holds a cached table or workspace.
+  std::lock_guard<std::mutex> g(ds->mu);
+  for (void* p : ds->retired) cudaFree(p);
+  ds->retired.clear();
+  for (auto& kv : ds->rope) {
+    cudaFree(kv.second.cs);
+    cudaFree(kv.second.sn);
+  }
+  ds->rope.clear();
+  for (auto& kv : ds->ws) cudaFree(kv.second.first);
+  ds->ws.clear();
   return FA_OK;
 }
 
@@ -1000,9 +1083,24 @@ fa_status fa_check_device_status(void) {
   FA_CUDA(cudaMemcpy(&v, ds->status, sizeof(v), cudaMemcpyDeviceToHost));
   if (v == 0) return FA_OK;
   FA_CUDA(cudaMemset(ds->status, 0, sizeof(unsigned)));
-  if (v & fa::FA_DEV_TIMEOUT)
-    return fail(FA_ERR_TIMEOUT, "a kernel wait exceeded its time limit; the kernel returned early and its output is invalid");
-  return fail(FA_ERR_RANGE, "an input value is outside the fp16 range used internally for bf16 inputs (|x| > 65504)");
+  return fail(FA_ERR_TIMEOUT, "a kernel wait exceeded its time limit; the kernel returned early and its output is invalid");
+}
+
+fa_status fa_set_wait_limit(double seconds) {
+  if (!(seconds > 0.0) || !(seconds <= 3600.0)) return fail(FA_ERR_INVALID_ARG, "wait limit must be in (0, 3600] s");
+  g_wait_limit_ns.store((unsigned long long)(seconds * 1e9), std::memory_order_relaxed);
+  return FA_OK;
+}
+
+double fa_get_wait_limit(void) {
+  const unsigned long long ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  return (ns ? (double)ns : (double)fa::kWaitLimitNs) * 1e-9;
+}
+
+fa_status fa_test_stall_next_launch(int32_t k_tile) {
+  if (k_tile < 0) return fail(FA_ERR_INVALID_ARG, "k_tile must be >= 0");
+  g_stall_k_tile = k_tile + 1;
+  return FA_OK;
 }
 
 uint64_t fa_launch_count(void) { return g_launches; }
@@ -1047,8 +1145,11 @@ const char* fa_last_error(void) { return g_last_error.c_str(); }
 // this library: code running inside a host application that owns every
 // device allocation (a plugin whose host forbids cudaMalloc, or a runtime
 // that budgets GPU memory up front). fa_forward_noalloc runs the same
-// kernels as fa_forward, but its scratch (the fp16 staging of Q/K/V and the
-// RoPE tables) lives in the fixed array below instead of a pool buffer.
+// dispatch and kernels as fa_forward, but its scratch (the staging record,
+// the fp16 staging of Q/K/V, padded operands for other head dims, and the
+// RoPE tables built from rope_theta) lives in the fixed array below instead
+// of a pool buffer, and its kernels report timeouts in a status word of
+// their own (fa_noalloc_check_status).
 //
 // The array is a file-scope __device__ variable of kNoAllocScratchBytes: every
 // GPU on which this module is loaded keeps it until the process exits. In
@@ -1056,10 +1157,11 @@ const char* fa_last_error(void) { return g_last_error.c_str(); }
 // taken with cudaGetSymbolAddress once per device (on the first call made
 // with that device current; make that first call before any stream
 // capture). All calls share the array and its contents persist between
-// calls; every byte a call reads is written earlier in the same call, so no
-// clearing is needed. Calls that may overlap on the GPU (different streams,
-// or several host threads) race on the array and must be serialised by the
-// caller.
+// calls: each call clears the staging record it needs at zero, and every
+// other byte it reads is written earlier in the same call. Calls that may
+// overlap on the GPU (different streams, or several host threads) race on
+// the array and must be serialised by the caller. Only the primary context
+// of each device is supported (the addresses are cached per device).
 namespace fa {
 namespace {
 
@@ -1068,15 +1170,45 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 static __device__ unsigned g_noalloc_status;  // kernel status bits of this entry point
 
 struct NoAllocDevice {
-  std::once_flag once;
-  cudaError_t err = cudaSuccess;
+  bool ready = false;
   unsigned char* scratch = nullptr;
   unsigned* status = nullptr;
 };
 constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
 NoAllocDevice g_noalloc_devices[kNoAllocMaxDevices];
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Device addresses of the array and the status word on the current device,
+// looked up once per device. A failed lookup is not cached, so a later call
+// (for example one made outside stream capture) tries again.
+fa_status noalloc_device(NoAllocDevice** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(FA_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
+  }
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(FA_ERR_INVALID_ARG, "device index out of range");
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  NoAllocDevice& nd = g_noalloc_devices[dev];
+  if (!nd.ready) {
+    unsigned char* scratch = nullptr;
+    unsigned* status = nullptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&scratch), g_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&status), g_noalloc_status);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return cuda_fail(e, "cudaGetSymbolAddress (allocation-free scratch)");
+    }
+    nd.scratch = scratch;
+    nd.status = status;
+    nd.ready = true;
+  }
+  *out = &nd;
+  return FA_OK;
+}
 
 }  // namespace
 }  // namespace fa
@@ -1089,10 +1221,6 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
   fa_status st = make_plan(p, &pl);
   if (st != FA_OK) return st;
   AttnArgs& a = pl.a;
-  if (pl.pad) {  // no padded staging here: other head dims take the CUDA-core kernel
-    pl.pad = false;
-    pl.ws_bytes = 0;
-  }
   const bool tables_from_theta = pl.rope && (cos == nullptr || sin == nullptr);
   const int rows = a.Sq > a.Sk ? a.Sq : a.Sk;
   const size_t table_bytes = tables_from_theta ? up256((size_t)rows * (a.D / 2) * sizeof(float)) : 0;
@@ -1103,100 +1231,42 @@ extern "C" fa_status fa_forward_noalloc(const fa_params* p, const void* q, const
                                         std::to_string(kNoAllocScratchBytes) + "-byte array (use fa_forward)");
   if (a.q_end <= a.q_begin || a.B == 0 || a.Hq == 0) return FA_OK;
   if (!o) return fail(FA_ERR_INVALID_ARG, "NULL output pointer");
-
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return fail(FA_ERR_NO_DEVICE, std::string("no CUDA device: ") + cudaGetErrorString(e));
-  }
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(FA_ERR_INVALID_ARG, "device index out of range");
-  NoAllocDevice& nd = g_noalloc_devices[dev];
-  std::call_once(nd.once, [&nd]() {
-    nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.scratch), g_noalloc_scratch);
-    if (nd.err == cudaSuccess) nd.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&nd.status), g_noalloc_status);
-  });
-  if (nd.err != cudaSuccess) return cuda_fail(nd.err, "cudaGetSymbolAddress(scratch)");
+  NoAllocDevice* nd = nullptr;
+  st = noalloc_device(&nd);
+  if (st != FA_OK) return st;
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_handle);
   a.o = o;
   a.lse = lse;
-  a.status = nd.status;
-  if (a.kv_end <= a.kv_begin) {
-    e = launch_fill_empty(a, pl.out_dtype, stream);
-    return e == cudaSuccess ? FA_OK : cuda_fail(e, "fill_empty");
-  }
-  if (!q || !k || !v) return fail(FA_ERR_INVALID_ARG, "NULL tensor pointer");
-
-  unsigned char* wp = nd.scratch;
+  unsigned char* wp = nd->scratch;
   const float* cs = cos;
   const float* sn = sin;
-  if (pl.rope && tables_from_theta) {
+  if (tables_from_theta && a.kv_end > a.kv_begin) {
     if (!(pl.rope_theta > 0.f) || !std::isfinite(pl.rope_theta))
       return fail(FA_ERR_INVALID_ARG, "has_rotary needs cos/sin tables or rope_theta > 0");
     if (a.D % 2 != 0) return fail(FA_ERR_UNSUPPORTED, "RoPE from rope_theta needs an even head_dim");
     float* tc = reinterpret_cast<float*>(wp);
     float* ts = reinterpret_cast<float*>(wp + table_bytes);
     wp += 2 * table_bytes;
-    e = launch_rope_table(tc, ts, rows, a.D, (double)pl.rope_theta, stream);
+    cudaError_t e = launch_rope_table(tc, ts, rows, a.D, (double)pl.rope_theta, stream);
     if (e != cudaSuccess) return cuda_fail(e, "rope tables");
     cs = tc;
     sn = ts;
   }
-  if (!pl.rope) cs = sn = nullptr;
+  // The rest of the array is the workspace (run() clears its staging record).
+  return run(pl, q, k, v, cs, sn, pl.ws_bytes ? wp : nullptr, pl.ws_bytes, stream, nullptr, nd->status);
+}
 
-  if (!pl.tc) {
-    a.q = q;
-    a.k = k;
-    a.v = v;
-    a.rope_cos = cs;
-    a.rope_sin = sn;
-    e = launch_attn_simt(a, pl.dtype, pl.out_dtype, stream);
-    return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (CUDA-core kernel)");
-  }
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return fail(FA_ERR_INVALID_ARG, "tensor base addresses must be 16-byte aligned");
-  const void* qs = q;
-  const void* ks = k;
-  const void* vs = v;
-  int64_t q_sb = a.q_sb, q_ss = a.q_ss, q_sh = a.q_sh;
-  int64_t k_sb = a.k_sb, k_ss = a.k_ss, k_sh = a.k_sh;
-  int64_t v_sb = a.v_sb, v_ss = a.v_ss, v_sh = a.v_sh;
-  bool qk_bf16 = (pl.dtype == kBF16);
-  if (pl.need_q16) {
-    __half* y = reinterpret_cast<__half*>(wp);
-    wp += up256((size_t)a.B * a.Sq * a.Hq * a.D * 2);
-    e = launch_prep_fp16(q, pl.dtype, a.q_sb, a.q_ss, a.q_sh, a.B, a.Sq, a.Hq, a.D, cs, sn, y, a.Sq, nd.status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep Q");
-    qs = y;
-    q_sb = (int64_t)a.Sq * a.Hq * a.D; q_ss = (int64_t)a.Hq * a.D; q_sh = a.D;
-  }
-  if (pl.need_k16) {
-    __half* y = reinterpret_cast<__half*>(wp);
-    wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(k, pl.dtype, a.k_sb, a.k_ss, a.k_sh, a.B, a.Sk, a.Hk, a.D, cs, sn, y, a.Sk, nd.status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep K");
-    ks = y;
-    k_sb = (int64_t)a.Sk * a.Hk * a.D; k_ss = (int64_t)a.Hk * a.D; k_sh = a.D;
-  }
-  if (pl.need_q16 || pl.need_k16) qk_bf16 = false;
-  if (pl.need_v16) {
-    __half* y = reinterpret_cast<__half*>(wp);
-    wp += up256((size_t)a.B * a.Sk * a.Hk * a.D * 2);
-    e = launch_prep_fp16(v, pl.dtype, a.v_sb, a.v_ss, a.v_sh, a.B, a.Sk, a.Hk, a.D, nullptr, nullptr, y,
-                         a.Sk, nd.status, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "prep V");
-    vs = y;
-    v_sb = (int64_t)a.Sk * a.Hk * a.D; v_ss = (int64_t)a.Hk * a.D; v_sh = a.D;
-  }
-  CUtensorMap tq, tk, tv;
-  st = encode_map(&tq, qs, qk_bf16, a.D, a.Hq, a.Sq, a.B, q_sb, q_ss, q_sh);
+extern "C" fa_status fa_noalloc_check_status(void) {
+  using namespace fa;
+  NoAllocDevice* nd = nullptr;
+  fa_status st = noalloc_device(&nd);
   if (st != FA_OK) return st;
-  st = encode_map(&tk, ks, qk_bf16, a.D, a.Hk, a.Sk, a.B, k_sb, k_ss, k_sh);
-  if (st != FA_OK) return st;
-  st = encode_map(&tv, vs, false, a.D, a.Hk, a.Sk, a.B, v_sb, v_ss, v_sh);
-  if (st != FA_OK) return st;
-  a.n_q_tiles = (a.q_end - a.q_begin + 127) / 128;
-  e = launch_attn_sm100(a, tq, tk, tv, qk_bf16, pl.out_dtype, stream);
-  return e == cudaSuccess ? FA_OK : cuda_fail(e, "attention (tensor-core kernel)");
+  unsigned v = 0;
+  FA_CUDA(cudaMemcpy(&v, nd->status, sizeof(v), cudaMemcpyDeviceToHost));
+  if (v == 0) return FA_OK;
+  FA_CUDA(cudaMemset(nd->status, 0, sizeof(unsigned)));
+  return fail(FA_ERR_TIMEOUT,
+              "a kernel wait of fa_forward_noalloc exceeded its time limit; the kernel returned early and its "
+              "output is invalid");
 }

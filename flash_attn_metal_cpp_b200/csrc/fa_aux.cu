@@ -1,12 +1,16 @@
 // fa_aux.cu - memory-bound helper kernels around the attention kernels:
-//   * prep_fp16:   rotate-half RoPE (common.metal:150-167) and/or conversion
-//                  to fp16, producing the contiguous fp16 operands the
-//                  tensor-core kernel loads with TMA;
+//   * stage / stage_fixup: rotate-half RoPE (common.metal:150-167) and/or
+//                  conversion to fp16 of Q, K and V in one launch, producing
+//                  the contiguous fp16 operands the tensor-core kernel loads
+//                  with TMA (zero-padded to 64 or 128 columns for other head
+//                  dims); a tensor whose values would overflow fp16 is
+//                  rescaled by a power of two, recorded for the kernel;
 //   * rope_table:  cos/sin tables [rows, D/2] (layout of the reference's
 //                  host tables, src/flash_attn_core.cpp:343-349), computed
 //                  in double and rounded to float;
 //   * combine:     merge of split-KV partials (O_j, LSE_j);
-//   * fill_empty:  O = 0, LSE = -inf when there is no key at all.
+//   * fill_empty:  O = 0, LSE = -inf when there is no key at all;
+//   * unpad:       first D columns of a padded output.
 #include "fa_internal.h"
 #include "fa_ptx.cuh"
 
@@ -52,81 +56,209 @@ __device__ __forceinline__ void load8<float>(const float* p, float (&x)[8]) {
   x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
 }
 
-__device__ __forceinline__ bool store8_half(__half* p, const float (&x)[8]) {
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p);
+template <>
+__device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
+
+// Largest finite value of fp16.
+constexpr float kHalfMax = 65504.f;
+
+// Stores 8 values as fp16; returns their largest magnitude (fmaxf drops NaN).
+__device__ __forceinline__ float store8_half(__half* p, const float (&x)[8]) {
   uint4 w;
   w.x = pack_half2(x[0], x[1]);
   w.y = pack_half2(x[2], x[3]);
   w.z = pack_half2(x[4], x[5]);
   w.w = pack_half2(x[6], x[7]);
   *reinterpret_cast<uint4*>(p) = w;
-  bool ok = true;
+  float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ok &= fabsf(x[i]) <= 65504.f;
-  return ok;
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(x[i]));
+  return m;
 }
 
-// One thread = 8 columns of the first half and (with RoPE) the matching 8
-// columns of the second half of one (b, s, h) row. Requires D % 16 == 0.
-template <typename T, bool ROPE>
-__global__ void prep_fp16_kernel(const T* __restrict__ x, int64_t sb, int64_t ss, int64_t sh, int S,
-                                 int H, int D, long long n_rows, const float* __restrict__ cs,
-                                 const float* __restrict__ sn, __half* __restrict__ y, int y_rows,
-                                 unsigned* status) {
-  const int chunks = ROPE ? D / 16 : D / 8;
-  const long long total = n_rows * chunks;
-  bool ok = true;
+// Value of output column `col` of row (b, s, h) of a staging job, before any
+// rescale: x (rotated over the pairs (i, i + D/2) of the original D when the
+// job has tables; an odd D's last column has no partner and is kept), zero
+// for the padding columns. Same rounding steps as rope_rotate8.
+template <typename T>
+__device__ __forceinline__ float stage_value(const StageJob& jb, int b, int s, int h, int col) {
+  if (col >= jb.D) return 0.f;
+  const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h * jb.sh;
+  const int half = jb.D / 2;
+  if (jb.cs != nullptr && col < 2 * half) {
+    const int i = col < half ? col : col - half;  // pair index
+    const float c = jb.cs[(int64_t)s * half + i], sv = jb.sn[(int64_t)s * half + i];
+    const float a0 = ld_f<T>(src + i), a1 = ld_f<T>(src + i + half);
+    return (col < half) ? __fmaf_rn(a0, c, -__fmul_rn(a1, sv)) : __fmaf_rn(a0, sv, __fmul_rn(a1, c));
+  }
+  return ld_f<T>(src + col);
+}
+
+// Work items of job j: 8-column chunks (16 with RoPE: 8 of each half) when
+// VEC, single elements of the Dp-wide output row otherwise.
+template <bool VEC>
+__device__ __forceinline__ long long job_items(const StageJob& jb) {
+  const long long rows = (long long)jb.B * jb.S * jb.H;
+  if (!VEC) return rows * jb.Dp;
+  return rows * (jb.cs != nullptr ? jb.D / 16 : jb.D / 8);
+}
+
+// Block-wide maximum of `v` (non-negative); the result is valid in thread 0.
+__device__ __forceinline__ float block_max(float v) {
+  __shared__ float part[32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) part[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0)
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i) v = fmaxf(v, part[i]);
+  return v;
+}
+
+// Staging pass over every job of the batch (one launch). VEC: each thread
+// converts 8 consecutive columns (and, with RoPE, the 8 partner columns of
+// the other half) with 16-byte loads and stores; requires Dp == D,
+// D % 16 == 0 with tables (D % 8 == 0 without) and 16-byte aligned rows.
+// Otherwise one thread per output element. Values are written unscaled; a
+// block whose largest magnitude exceeds the fp16 range records it in
+// rec->amax_bits (the fixup kernel then rewrites that tensor).
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(256) stage_kernel(const StageBatch bt) {
+  // Work items of the jobs, back to back: job 0 ends at e1, job 1 at e2.
+  const long long e1 = bt.n > 0 ? job_items<VEC>(bt.job[0]) : 0;
+  const long long e2 = e1 + (bt.n > 1 ? job_items<VEC>(bt.job[1]) : 0);
+  const long long total = e2 + (bt.n > 2 ? job_items<VEC>(bt.job[2]) : 0);
+  float am0 = 0.f, am1 = 0.f, am2 = 0.f;  // largest magnitude per job
   for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
        idx += (long long)gridDim.x * blockDim.x) {
-    const long long rowi = idx / chunks;
-    const int ch = (int)(idx - rowi * chunks);
-    const int h = (int)(rowi % H);
-    const long long bs = rowi / H;
-    const int s = (int)(bs % S);
-    const int b = (int)(bs / S);
-    const T* src = x + (int64_t)b * sb + (int64_t)s * ss + (int64_t)h * sh;
-    __half* dst = y + (((int64_t)b * y_rows + s) * H + h) * D;  // y: [B, y_rows, H, D]
-    if (ROPE) {
-      const int half = D / 2;
-      const int c0 = ch * 8;
-      float a[8], bb[8];
-      load8<T>(src + c0, a);
-      load8<T>(src + c0 + half, bb);
-      const float4* cp = reinterpret_cast<const float4*>(cs + (int64_t)s * half + c0);
-      const float4* sp = reinterpret_cast<const float4*>(sn + (int64_t)s * half + c0);
-      const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
-      const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
-      const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
-      float ra[8], rb[8];
-      rope_rotate8(a, bb, cv, sv, ra, rb);
-      ok &= store8_half(dst + c0, ra);
-      ok &= store8_half(dst + c0 + half, rb);
+    const int j = idx < e1 ? 0 : (idx < e2 ? 1 : 2);
+    const StageJob& jb = bt.job[j];
+    const long long li = idx - (j == 0 ? 0 : (j == 1 ? e1 : e2));
+    float m;
+    if constexpr (VEC) {
+      const bool rope = jb.cs != nullptr;
+      const int chunks = rope ? jb.D / 16 : jb.D / 8;
+      const long long rowi = li / chunks;
+      const int ch = (int)(li - rowi * chunks);
+      const int h = (int)(rowi % jb.H);
+      const long long bs = rowi / jb.H;
+      const int s = (int)(bs % jb.S);
+      const int b = (int)(bs / jb.S);
+      const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h * jb.sh;
+      __half* dst = jb.y + (((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.D;
+      if (rope) {
+        const int half = jb.D / 2;
+        const int c0 = ch * 8;
+        float a[8], bb[8];
+        load8<T>(src + c0, a);
+        load8<T>(src + c0 + half, bb);
+        const float4* cp = reinterpret_cast<const float4*>(jb.cs + (int64_t)s * half + c0);
+        const float4* sp = reinterpret_cast<const float4*>(jb.sn + (int64_t)s * half + c0);
+        const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
+        const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+        const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
+        float ra[8], rb[8];
+        rope_rotate8(a, bb, cv, sv, ra, rb);
+        m = fmaxf(store8_half(dst + c0, ra), store8_half(dst + c0 + half, rb));
+      } else {
+        float a[8];
+        load8<T>(src + ch * 8, a);
+        m = store8_half(dst + ch * 8, a);
+      }
     } else {
-      float a[8];
-      load8<T>(src + ch * 8, a);
-      ok &= store8_half(dst + ch * 8, a);
+      const int col = (int)(li % jb.Dp);
+      const long long rowi = li / jb.Dp;
+      const int h = (int)(rowi % jb.H);
+      const long long bs = rowi / jb.H;
+      const int s = (int)(bs % jb.S);
+      const int b = (int)(bs / jb.S);
+      const float val = stage_value<T>(jb, b, s, h, col);
+      m = fmaxf(0.f, fabsf(val));
+      jb.y[(((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.Dp + col] = __float2half_rn(val);
     }
+    if (j == 0) am0 = fmaxf(am0, m);
+    else if (j == 1) am1 = fmaxf(am1, m);
+    else am2 = fmaxf(am2, m);
   }
-  if (!ok) atomicOr(status, FA_DEV_RANGE);
+  // Only magnitudes beyond the fp16 range matter to the fixup: other blocks
+  // skip the atomic.
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    if (j >= bt.n) break;
+    const float aj = (j == 0) ? am0 : ((j == 1) ? am1 : am2);
+    const float m = block_max(aj > kHalfMax ? aj : 0.f);
+    if (threadIdx.x == 0 && m > kHalfMax) atomicMax(&bt.rec->amax_bits[bt.job[j].slot], __float_as_uint(m));
+  }
 }
 
+// Exponent e >= 0 with amax * 2^-e <= 65504 (0 when amax is in range, or is
+// inf / NaN: such inputs propagate as they would in fp32 arithmetic).
+__device__ __forceinline__ int range_exponent(float amax) {
+  if (!(amax > kHalfMax) || !isfinite(amax)) return 0;
+  int e = 0;
+  frexpf(amax / kHalfMax, &e);  // amax / 65504 = m * 2^e, m in [0.5, 1)
+  return min(e, 126);
+}
+
+// Second half of the staging pass. Every block reads the recorded maxima;
+// if none was recorded (the usual case) block 0 publishes zero exponents and
+// every block exits. Otherwise each tensor with a finite maximum beyond the
+// fp16 range is rewritten as round_fp16(value * 2^-e) from its source, and
+// the last block to finish clears the maxima for the next call.
 template <typename T>
-cudaError_t prep_t(const void* x, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H, int D,
-                   const float* cs, const float* sn, __half* y, int y_rows, unsigned* status,
-                   cudaStream_t st) {
-  const long long n_rows = (long long)B * S * H;
-  const long long total = n_rows * (cs ? D / 16 : D / 8);
-  if (total == 0) return cudaSuccess;
-  const int threads = 256;
-  long long blocks = (total + threads - 1) / threads;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  if (cs)
-    prep_fp16_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(
-        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, y_rows, status);
-  else
-    prep_fp16_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(
-        reinterpret_cast<const T*>(x), sb, ss, sh, S, H, D, n_rows, cs, sn, y, y_rows, status);
-  note_launch();
-  return cudaGetLastError();
+__global__ void __launch_bounds__(256) stage_fixup_kernel(const StageBatch bt) {
+  __shared__ int s_exp[3];
+  __shared__ int s_recorded;
+  RangeRec* rec = bt.rec;
+  if (threadIdx.x == 0) {
+    unsigned recorded = 0;
+    for (int slot = 0; slot < 3; ++slot) {
+      const unsigned bits = __ldcg(&rec->amax_bits[slot]);
+      recorded |= bits;
+      s_exp[slot] = range_exponent(__uint_as_float(bits));
+    }
+    s_recorded = recorded != 0u;
+    if (blockIdx.x == 0)
+      for (int slot = 0; slot < 4; ++slot) rec->exp[slot] = slot < 3 ? s_exp[slot] : 0;
+  }
+  __syncthreads();
+  if (!s_recorded) return;
+  for (int j = 0; j < bt.n; ++j) {
+    const StageJob& jb = bt.job[j];
+    const int e = s_exp[jb.slot];
+    if (e == 0) continue;
+    const float mul = __int_as_float((127 - e) << 23);  // 2^-e, exact
+    const long long total = (long long)jb.B * jb.S * jb.H * jb.Dp;
+    for (long long li = blockIdx.x * (long long)blockDim.x + threadIdx.x; li < total;
+         li += (long long)gridDim.x * blockDim.x) {
+      const int col = (int)(li % jb.Dp);
+      const long long rowi = li / jb.Dp;
+      const int h = (int)(rowi % jb.H);
+      const long long bs = rowi / jb.H;
+      const int s = (int)(bs % jb.S);
+      const int b = (int)(bs / jb.S);
+      const float val = stage_value<T>(jb, b, s, h, col);
+      jb.y[(((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.Dp + col] = __float2half_rn(__fmul_rn(val, mul));
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(&rec->done, 1u) == gridDim.x - 1) {
+      // Every block has read the maxima: clear them for the next call.
+      for (int slot = 0; slot < 4; ++slot) rec->amax_bits[slot] = 0u;
+      rec->done = 0u;
+      __threadfence();
+    }
+  }
 }
 
 __global__ void rope_table_kernel(float* cs, float* sn, int rows, int D, double theta) {
@@ -235,54 +367,6 @@ __global__ void fill_empty_kernel(const AttnArgs a) {
   }
 }
 
-template <typename T>
-__device__ __forceinline__ float ld_f(const T* p);
-template <>
-__device__ __forceinline__ float ld_f<__half>(const __half* p) { return __half2float(*p); }
-template <>
-__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
-template <>
-__device__ __forceinline__ float ld_f<float>(const float* p) { return *p; }
-
-// Zero-padded fp16 staging for head dims the tensor-core kernel does not take
-// natively: y[.., 0:D] = rope(x) with the pairs (i, i + D/2) of the ORIGINAL
-// D (an odd D's last column has no partner and is kept, as in the oracle),
-// y[.., D:Dp] = 0, so every dot product is unchanged. One thread per output
-// element of rows [0, S); y is contiguous [B, y_rows, H, Dp].
-template <typename T>
-__global__ void prep_pad_kernel(const T* __restrict__ x, int64_t sb, int64_t ss, int64_t sh, int S, int H, int D,
-                                int Dp, long long n_rows, const float* __restrict__ cs,
-                                const float* __restrict__ sn, __half* __restrict__ y, int y_rows,
-                                unsigned* status) {
-  const long long total = n_rows * Dp;
-  const int half = D / 2;
-  bool ok = true;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int col = (int)(idx % Dp);
-    const long long rowi = idx / Dp;
-    const int h = (int)(rowi % H);
-    const long long bs = rowi / H;
-    const int s = (int)(bs % S);
-    const int b = (int)(bs / S);
-    const T* src = x + (int64_t)b * sb + (int64_t)s * ss + (int64_t)h * sh;
-    float val = 0.f;
-    if (col < D) {
-      val = ld_f<T>(src + col);
-      if (cs != nullptr && col < 2 * half) {
-        const int i = col < half ? col : col - half;  // pair index
-        const float c = cs[(int64_t)s * half + i], sv = sn[(int64_t)s * half + i];
-        const float a0 = ld_f<T>(src + i), a1 = ld_f<T>(src + i + half);
-        // same rounding steps as rope_rotate8
-        val = (col < half) ? __fmaf_rn(a0, c, -__fmul_rn(a1, sv)) : __fmaf_rn(a0, sv, __fmul_rn(a1, c));
-      }
-      ok &= fabsf(val) <= 65504.f;
-    }
-    y[(((int64_t)b * y_rows + s) * H + h) * Dp + col] = __float2half_rn(val);
-  }
-  if (!ok) atomicOr(status, FA_DEV_RANGE);
-}
-
 // O[b, q, h, 0:D] = O_pad[b, q, h, 0:D] for rows [q_begin, q_end); O_pad is
 // contiguous [B, Sq, H, Dp], O has element strides (sb, ss, sh). Element size
 // 2 or 4 bytes (the output dtype).
@@ -303,32 +387,42 @@ __global__ void unpad_kernel(const E* __restrict__ src, E* __restrict__ dst, int
   }
 }
 
-}  // namespace
-
-cudaError_t launch_prep_pad(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H,
-                            int D, int Dp, const float* cs, const float* sn, __half* y, int y_rows, unsigned* status,
-                            cudaStream_t st) {
-  const long long n_rows = (long long)B * S * H;
-  const long long total = n_rows * Dp;
-  if (total == 0) return cudaSuccess;
-  long long blocks = (total + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  switch (in_dtype) {
-    case kF16:
-      prep_pad_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const __half*>(x), sb, ss, sh, S,
-                                                                H, D, Dp, n_rows, cs, sn, y, y_rows, status);
-      break;
-    case kBF16:
-      prep_pad_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
-          reinterpret_cast<const __nv_bfloat16*>(x), sb, ss, sh, S, H, D, Dp, n_rows, cs, sn, y, y_rows, status);
-      break;
-    default:
-      prep_pad_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const float*>(x), sb, ss, sh, S,
-                                                               H, D, Dp, n_rows, cs, sn, y, y_rows, status);
-      break;
+template <typename T>
+cudaError_t stage_t(const StageBatch& bt, cudaStream_t st) {
+  bool vec = true;
+  long long items = 0;
+  for (int j = 0; j < bt.n; ++j) {
+    const StageJob& jb = bt.job[j];
+    const int need = jb.cs ? 16 : 8;
+    vec &= (jb.Dp == jb.D) && (jb.D % need == 0);
+    items += (long long)jb.B * jb.S * jb.H * jb.Dp;
   }
+  if (items == 0) return cudaSuccess;
+  const int threads = 256;
+  long long blocks = (items / (vec ? 8 : 1) + threads - 1) / threads;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (vec)
+    stage_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(bt);
+  else
+    stage_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(bt);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // One block per SM: when nothing overflowed every block reads 16 bytes and exits.
+  stage_fixup_kernel<T><<<148, threads, 0, st>>>(bt);
   note_launch();
   return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_stage(const StageBatch& bt, cudaStream_t st) {
+  if (bt.n <= 0) return cudaSuccess;
+  switch (bt.in_dtype) {
+    case kF16: return stage_t<__half>(bt, st);
+    case kBF16: return stage_t<__nv_bfloat16>(bt, st);
+    default: return stage_t<float>(bt, st);
+  }
 }
 
 cudaError_t launch_unpad(const void* src, void* dst, int elem_bytes, int64_t sb, int64_t ss, int64_t sh, int B,
@@ -346,16 +440,6 @@ cudaError_t launch_unpad(const void* src, void* dst, int elem_bytes, int64_t sb,
                                                               Dp, q_begin, q_end);
   note_launch();
   return cudaGetLastError();
-}
-
-cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B,
-                             int S, int H, int D, const float* cs, const float* sn, __half* y,
-                             int y_rows, unsigned* status, cudaStream_t st) {
-  switch (in_dtype) {
-    case kF16: return prep_t<__half>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
-    case kBF16: return prep_t<__nv_bfloat16>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
-    default: return prep_t<float>(x, sb, ss, sh, B, S, H, D, cs, sn, y, y_rows, status, st);
-  }
 }
 
 cudaError_t launch_rope_table(float* cs, float* sn, int rows, int D, double theta, cudaStream_t st) {

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const unsigned long long wlim = a.wait_limit_ns ? a.wait_limit_ns : kWaitLimitNs;
 
   // Work item: heaviest causal blocks first, heads of one KV group adjacent.
   const int n_blocks = (a.q_end - a.q_begin + NT * BM - 1) / (NT * BM);
@@ -248,14 +249,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_4d(sQ + t * C::TILE_BYTES + bx * C::BOX_BYTES, &tm_q, bq, bx * 64, hq, q0 + t * BM, bz);
         }
       }
+      // Test hook (AttnArgs::skip_k_tile): CTA 0 never loads one K tile, so
+      // the MMA thread's wait for it runs out and the kernel takes its abort
+      // path. Off (0) in every production launch.
+      const int skip_j = (is_k && blockIdx.x == 0) ? a.skip_k_tile - 1 : -1;
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         if (*abort_flag) break;
         const int st = j % C::NS;
-        if (!fa_wait(smem_addr(&empty[st]), ((j / C::NS) + 1) & 1, a.status)) {
+        if (!fa_wait(smem_addr(&empty[st]), ((j / C::NS) + 1) & 1, a.status, wlim)) {
           *abort_flag = 1;
           break;
         }
+        if (j == skip_j) continue;
         const uint32_t bfull = smem_addr(&full[st]);
         mbar_arrive_expect_tx(bfull, C::TILE_BYTES);
 #pragma unroll
@@ -268,10 +274,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (is_k) {
 #pragma unroll
         for (int t = 0; t < NT; ++t)
-          if (n_kv_t[t] > 0) fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
+          if (n_kv_t[t] > 0) fa_wait(smem_addr(&bars->q_full[t]), 0, a.status, wlim);
       }
       for (int j = max(0, issued - C::NS); j < issued; ++j)
-        fa_wait(smem_addr(&full[j % C::NS]), (j / C::NS) & 1, a.status);
+        if (j != skip_j) fa_wait(smem_addr(&full[j % C::NS]), (j / C::NS) & 1, a.status, wlim);
     } else if (warp == kMmaWarp && lane == 0 && n_kv > 0) {
       // -------------------------------------------------------- MMA issuer
       constexpr uint32_t fmt_qk = QK_BF16 ? 1u : 0u;
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
-        if (ok && n_kv_t[t] > 0) ok = fa_wait(smem_addr(&bars->q_full[t]), 0, a.status);
+        if (ok && n_kv_t[t] > 0) ok = fa_wait(smem_addr(&bars->q_full[t]), 0, a.status, wlim);
       // j runs one past the last KV tile to issue the final PV of each tile.
       for (int j = 0; ok && j <= n_kv; ++j) {
         if (*abort_flag) { ok = false; break; }
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int i = j - 1;
             const int it = i - s_lo[t];  // this tile's step
             if (!v_ready) {
-              if (!fa_wait(smem_addr(&bars->v_full[i % C::NS]), (i / C::NS) & 1, a.status)) { ok = false; break; }
+              if (!fa_wait(smem_addr(&bars->v_full[i % C::NS]), (i / C::NS) & 1, a.status, wlim)) { ok = false; break; }
               v_ready = true;
             }
             // 16 keys x D cols per MMA: D-halves C::BOX_BYTES apart (LBO), 8-key groups 1024 B (SBO).
@@ -309,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t v_lo = v_lo0 + (uint32_t)((i % C::NS) * C::TILE_BYTES >> 4);
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
-              if (!fa_wait(smem_addr(&bars->p_full[t][half]), it & 1, a.status)) { ok = false; break; }
+              if (!fa_wait(smem_addr(&bars->p_full[t][half]), it & 1, a.status, wlim)) { ok = false; break; }
               tc_fence_after();
 #pragma unroll
               for (int kk = half * 4; kk < half * 4 + 4; ++kk)
@@ -321,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j >= s_lo[t] && j < s_lo[t] + n_kv_t[t]) {
             // S_t = Q_t K_j^T.
             if (!k_ready) {
-              if (!fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status)) { ok = false; break; }
+              if (!fa_wait(smem_addr(&bars->k_full[j % C::NS]), (j / C::NS) & 1, a.status, wlim)) { ok = false; break; }
               k_ready = true;
             }
             tc_fence_after();
@@ -342,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) *abort_flag = 1;
       // All MMAs of this CTA must be complete before TMEM is released.
       mma_commit(smem_addr(&bars->mma_final));
-      fa_wait(smem_addr(&bars->mma_final), 0, a.status);
+      fa_wait(smem_addr(&bars->mma_final), 0, a.status, wlim);
     }
   } else {
     // ------------------------------------------------------------ softmax warpgroups
@@ -353,22 +359,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_kv = (t == 0) ? n_kv_t[0] : n_kv_t[1];  // t is not a constant here
     const int my_lo = EXT ? j_min + ((t == 0) ? s_lo[0] : s_lo[1]) : 0;  // absolute first KV tile
     const int r_tile = q0 + t * BM;
+    // The staging pass may have stored Q, K, V as x * 2^-e (e >= 0) to keep
+    // them inside the fp16 range: the raw scores are then S * 2^-(e_q + e_k)
+    // and O comes out 2^-e_v too small. Fold both back (exact powers of two).
+    float sl2 = a.scale_log2, scale_raw = a.scale, o_mul = 1.f;
+    if (a.range_exp != nullptr) {
+      const int eq = a.range_exp[0], ek = a.range_exp[1], ev = a.range_exp[2];
+      const float fq = __int_as_float((127 + eq) << 23), fk = __int_as_float((127 + ek) << 23);
+      sl2 = sl2 * fq * fk;
+      scale_raw = scale_raw * fq * fk;
+      o_mul = __int_as_float((127 + ev) << 23);
+    }
     // ALiBi (common.metal:123-128): slope * (k - q) on the scaled score, folded
     // into the raw score as (slope / scale) * (k - q) (scale != 0 on this path).
-    const float slope_raw = (EXT && a.alibi != nullptr) ? a.alibi[hq] / a.scale : 0.f;
+    const float slope_raw = (EXT && a.alibi != nullptr) ? a.alibi[hq] / scale_raw : 0.f;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t tS = lane_base + kColS + t * 128;
     const uint32_t tO = lane_base + kColO + t * 128;
     const uint32_t b_s_full = smem_addr(&bars->s_full[t]);
     const uint32_t b_p_full = smem_addr(&bars->p_full[t][0]);  // [t][1] is 8 bytes further
-    const float sl2 = a.scale_log2;
     float m_run = -INFINITY;  // running max in log2 units (value actually subtracted)
     float l_run = 0.f;
     bool ok = true;
 
     for (int j = 0; j < my_kv; ++j) {
       if (*abort_flag) { ok = false; break; }
-      const bool got = fa_wait(b_s_full, j & 1, a.status);
+      const bool got = fa_wait(b_s_full, j & 1, a.status, wlim);
       if (!__all_sync(0xffffffffu, got)) { ok = false; *abort_flag = 1; break; }
       tc_fence_after();
       float s[BN];
@@ -469,12 +485,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- epilogue
     const bool row_ok = (row_g < a.q_end) && (q0 + t * BM < a.q_end);
     if (ok && my_kv > 0) {
-      const bool got = fa_wait(smem_addr(&bars->o_full[t]), 0, a.status);
+      const bool got = fa_wait(smem_addr(&bars->o_full[t]), 0, a.status, wlim);
       if (!__all_sync(0xffffffffu, got)) { ok = false; *abort_flag = 1; }
       tc_fence_after();
     }
     if (ok && q0 + t * BM < a.q_end) {
-      const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+      const float inv_l = (l_run > 0.f) ? o_mul / l_run : 0.f;
       // Routed slots are a multiple of BM rows, so the tile's first row
       // names the owner of all its rows.
       RowDst dst = row_dst(a, q0 + t * BM);

@@ -34,7 +34,16 @@ struct AttnArgs {
   float* lse;              // [B, Hq, Sq] (NULL = not written)
   const float* rope_cos;   // [rows, D/2] (SIMT kernel applies RoPE on load when non-NULL)
   const float* rope_sin;
-  unsigned* status;        // device status word (timeouts, range errors)
+  unsigned* status;        // device status word (timeouts)
+  // Power-of-two exponents (Q, K, V) by which the staging pass scaled the
+  // fp16 operands down to keep them finite (RangeRec::exp; NULL = none):
+  // scores are multiplied by 2^(e_q + e_k) and O by 2^e_v.
+  const int* range_exp;
+  // Limit of every in-kernel wait in nanoseconds (0 = the default limit).
+  unsigned long long wait_limit_ns;
+  // Test hook: when > 0, the K producer of the CTA working on blockIdx.x 0
+  // never loads K tile (skip_k_tile - 1), so the waits for it run out.
+  int skip_k_tile;
   // Routed output (split-KV across devices): when route_rows > 0, query row r
   // is owned by owner r / route_rows and its O / LSE go to that owner's
   // staging slot instead of o / lse: route[owner] is the slot's O base
@@ -84,19 +93,46 @@ cudaError_t launch_attn_sm100(const AttnArgs& a, const CUtensorMap& tq, const CU
 // Generic CUDA-core path: any head_dim <= 256, fp32/fp16/bf16 inputs.
 cudaError_t launch_attn_simt(const AttnArgs& a, int in_dtype, int out_dtype, cudaStream_t stream);
 
-// RoPE / format pre-pass over S rows: y = rope(x) (if cos != NULL) converted
-// to fp16. x has strides (sb, ss, sh); y is contiguous [B, y_rows, H, D]
-// (y_rows >= S, so a row range of a larger tensor can be staged in place).
-// Row s uses table row s of cos/sin.
-cudaError_t launch_prep_fp16(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh,
-                             int B, int S, int H, int D, const float* cos, const float* sin,
-                             __half* y, int y_rows, unsigned* status, cudaStream_t stream);
+// Per-call record of the fp16 staging pass, at the start of the workspace.
+// It must be zero before the first call that uses it; the staging kernels
+// leave it zero again (amax and done) when they finish.
+struct RangeRec {
+  unsigned amax_bits[4];   // max |value| staged per tensor (Q, K, V), as float bits
+  int exp[4];              // exponent e: the staged tensor holds value * 2^-e
+  unsigned done;           // fixup blocks finished; the last one resets amax and done
+};
+constexpr size_t kRangeRecBytes = 256;
+static_assert(sizeof(RangeRec) <= kRangeRecBytes, "range record");
 
-// Zero-padded fp16 staging (head dim D -> Dp in {64, 128}) with RoPE on the
-// original D's pairs; y is contiguous [B, y_rows, H, Dp].
-cudaError_t launch_prep_pad(const void* x, int in_dtype, int64_t sb, int64_t ss, int64_t sh, int B, int S, int H,
-                            int D, int Dp, const float* cos, const float* sin, __half* y, int y_rows,
-                            unsigned* status, cudaStream_t stream);
+// One tensor staged as fp16 for the tensor-core kernel: y = rope(x) (when
+// cs != NULL; rotate-half over the pairs (i, i + D/2) of the original D)
+// converted to fp16 with Dp - D zero columns appended. x has element
+// strides (sb, ss, sh) and S rows starting at its row 0; y is contiguous
+// [B, y_rows, H, Dp] at the same row offset, so a row range of a larger
+// tensor can be staged in place. Row s uses table row s of cs / sn.
+struct StageJob {
+  const void* x;
+  int64_t sb, ss, sh;
+  int B, S, H, D, Dp;
+  const float* cs;
+  const float* sn;
+  __half* y;
+  int y_rows;
+  int slot;                // 0 = Q, 1 = K, 2 = V (index into RangeRec)
+};
+
+struct StageBatch {
+  StageJob job[3];
+  int n;
+  int in_dtype;
+  RangeRec* rec;           // device record (zeroed before its first use)
+};
+
+// Stage every job of `b` (one kernel) and, in a second kernel, rescale a
+// tensor whose largest value would overflow fp16 (|x| > 65504) by the
+// smallest power of two that keeps it finite; the exponents land in
+// b.rec->exp for the attention kernel (AttnArgs::range_exp).
+cudaError_t launch_stage(const StageBatch& b, cudaStream_t stream);
 
 // Copy the first D of Dp columns of a contiguous padded O into O (strides in
 // elements), rows [q_begin, q_end); elem_bytes 2 or 4.

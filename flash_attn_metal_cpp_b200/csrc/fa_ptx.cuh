@@ -16,11 +16,12 @@ namespace fa {
 // Status bits written by kernels into the per-device status word.
 enum : unsigned {
   FA_DEV_TIMEOUT = 1u,
-  FA_DEV_RANGE = 2u,
 };
 
-// Wall-clock limit of any single in-kernel wait (nanoseconds). A correct
-// wait lasts microseconds; this only ends a kernel whose partner is gone.
+// Default wall-clock limit of any single in-kernel wait (nanoseconds). A
+// correct wait lasts microseconds; this only ends a kernel whose partner is
+// gone. Callers can set another limit (fa_set_wait_limit); kernels take it
+// from AttnArgs::wait_limit_ns.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -84,13 +85,14 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parit
 }
 
 // Wait until the phase with parity `parity` of barrier `bar` has completed.
-// Returns false (and records a timeout in *status) if the limit ran out.
-__device__ __forceinline__ bool fa_wait(uint32_t bar, uint32_t parity, unsigned* status) {
+// Returns false (and records a timeout in *status) if `limit_ns` ran out.
+__device__ __forceinline__ bool fa_wait(uint32_t bar, uint32_t parity, unsigned* status,
+                                        unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicOr(status, FA_DEV_TIMEOUT);
       return false;
     }

@@ -35,6 +35,22 @@ from . import _flash_attn_metal as _ext
 from . import sharding
 
 
+class PeerLostError(RuntimeError):
+    """A rank of a split-KV group left (or stopped answering) before the merge."""
+
+
+def merge_barrier(flag: torch.Tensor, group=None) -> None:
+    """The one collective of a split-KV step: after it, every rank's partial
+    kernel (and its peer stores into the owners' staging) precedes every
+    owner's merge in stream order. A peer that exited or never arrives makes
+    the backend raise (connection closed, or the process group's timeout);
+    that is reported as PeerLostError so no owner merges stale staging."""
+    try:
+        dist.all_reduce(flag, group=group)
+    except Exception as exc:  # gloo: closed connection / timeout; NCCL: communicator error
+        raise PeerLostError(f"split-KV merge barrier failed: a peer rank left or did not arrive ({exc})") from exc
+
+
 class _DeviceArray:
     """Zero-copy torch view of raw device memory (CUDA array interface)."""
 
@@ -135,7 +151,7 @@ class SplitKVAttention:
                                out_dtype=torch.float32, route=self._routes[buf], n_owners=p.n_owners,
                                owner_rows=p.owner_rows, window_size=window_size, alibi_slopes=alibi_slopes)
         # Every partial kernel precedes every owner's merge (stream-ordered).
-        dist.all_reduce(self._flag, group=self.group)
+        merge_barrier(self._flag, self.group)
         lo, hi = p.owner_block(self.rank)
         rows = hi - lo
         odt = q.dtype if out_dtype is None else out_dtype
@@ -168,7 +184,8 @@ class QShardAttention:
     needs no merge): rank r computes row chunks r and 2W-1-r of 2W against
     every visible key, the two chunks as concurrent launches on two streams.
     No collective touches the data. `forward` writes the rank's rows into a
-    (B, Sq, Hq, D) output and leaves the other rows untouched."""
+    (B, Sq, Hq, D) output (of any of the three dtypes) and leaves the other
+    rows untouched."""
 
     def __init__(self, seqlen_q: int, rank: int, world: int, device: Optional[torch.device] = None):
         self.rank, self.world = rank, world
@@ -181,7 +198,7 @@ class QShardAttention:
                 alibi_slopes=None) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
         kw = dict(softmax_scale=softmax_scale, is_causal=causal, cos=cos, sin=sin, rope_theta=rope_theta,
-                  window_size=window_size, alibi_slopes=alibi_slopes)
+                  window_size=window_size, alibi_slopes=alibi_slopes, out_dtype=out.dtype)
         Sk = k.shape[1]
         self._side.wait_stream(main)  # inputs written on the main stream are ready
         for i, (lo, hi) in enumerate(self.ranges):

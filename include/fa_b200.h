@@ -60,7 +60,8 @@ typedef enum fa_status {
     FA_ERR_UNSUPPORTED = 2,   /* valid request that this build does not implement */
     FA_ERR_CUDA = 3,          /* a CUDA runtime/driver call failed */
     FA_ERR_TIMEOUT = 4,       /* a bounded in-kernel wait ran out (kernel returned early) */
-    FA_ERR_RANGE = 5,         /* a value left the range of the internal fp16 format */
+    FA_ERR_RANGE = 5,         /* reserved: no longer returned (operands beyond the fp16
+                                 range are rescaled by a power of two, see fa_forward) */
     FA_ERR_NOT_INITIALIZED = 6,
     FA_ERR_NO_DEVICE = 7
 } fa_status;
@@ -136,7 +137,12 @@ size_t fa_tensor_bytes(uint32_t batch, uint32_t seq, uint32_t heads,
  *               row = position (layout of src/flash_attn_core.cpp:343-349);
  *               NULL with has_rotary set = build from rope_theta
  *   workspace : device scratch of fa_workspace_size(p) bytes, or NULL to use
- *               the library's cached per-device pool. */
+ *               the library's cached per-stream workspace.
+ * On the tensor-core path, fp16/bf16 operands are staged as fp16 (RoPE
+ * applied, bf16 converted); a staged tensor whose largest magnitude exceeds
+ * 65504 is stored scaled by the smallest power of two 2^-e that keeps it
+ * finite, and the kernel multiplies the scores (Q, K) or O (V) back by 2^e,
+ * so inputs anywhere in the bf16 range give correct results. */
 fa_status fa_forward(const fa_params* p, const void* q, const void* k,
                      const void* v, void* o, float* lse, const float* cos,
                      const float* sin, void* workspace, size_t workspace_bytes,
@@ -231,13 +237,32 @@ fa_status fa_rope_tables(float* cos_out, float* sin_out, uint32_t rows,
 /* Device-pool statistics of the calling thread's current device. */
 fa_status fa_pool_stats(uint64_t* hits, uint64_t* misses, uint64_t* bytes_reserved);
 
-/* Free every cached buffer of the calling thread's current device. */
+/* Synchronise the calling thread's current device, then free every cached
+ * buffer of it: the host-path pool, the per-stream workspaces of fa_forward
+ * calls made without one, the RoPE tables built from rope_theta, and the
+ * buffers those caches replaced when they grew. Calls in flight on other
+ * host threads must have finished enqueuing. */
 fa_status fa_pool_clear(void);
 
 /* Read and clear the in-kernel status word of the current device (after the
- * stream has been synchronised). Returns FA_ERR_TIMEOUT or FA_ERR_RANGE when
- * a kernel recorded one since the last call, else FA_OK. */
+ * stream has been synchronised). Returns FA_ERR_TIMEOUT when a kernel of
+ * this library (other than fa_forward_noalloc's) gave up a wait since the
+ * last call, else FA_OK. */
 fa_status fa_check_device_status(void);
+
+/* Wall-clock limit of every in-kernel wait of later launches, in seconds
+ * (default 2 s; process-wide). A wait that runs out makes its kernel record
+ * FA_ERR_TIMEOUT, release its resources and return early. Raise it when the
+ * GPU is time-sliced with other work for long periods. */
+fa_status fa_set_wait_limit(double seconds);
+double fa_get_wait_limit(void);
+
+/* Test hook (no counterpart in the reference): the next tensor-core launch
+ * of the calling thread withholds K tile `k_tile` (counted from the first
+ * key tile) from its first CTA, so that CTA's waits run out after the wait
+ * limit and the kernel takes its timeout path; the status word then reads
+ * FA_ERR_TIMEOUT. Only tests use it. */
+fa_status fa_test_stall_next_launch(int32_t k_tile);
 
 /* Number of kernels this library launched on the calling thread so far. */
 uint64_t fa_launch_count(void);
@@ -258,20 +283,28 @@ const char* fa_last_error(void);
  * application that owns every device allocation and forbids cudaMalloc.
  * Same arguments and results as fa_forward without the workspace: the caller
  * passes device inputs and outputs, and the library's scratch (fp16 staging
- * of Q/K/V, RoPE tables built from rope_theta) lives in one fixed 64 MiB
- * device array that every GPU loading the library's module keeps until the
- * process exits. Calls no cudaMalloc/cudaFree and no allocating library
- * routine. A problem whose scratch exceeds 64 MiB is rejected with
- * FA_ERR_INVALID_ARG and a message giving the size it needs.
+ * of Q/K/V, zero-padded operands and output for head dims other than 64 and
+ * 128, RoPE tables built from rope_theta) lives in one fixed 64 MiB device
+ * array that every GPU loading the library's module keeps until the process
+ * exits. Calls no cudaMalloc/cudaFree and no allocating library routine.
+ * A problem whose scratch exceeds 64 MiB is rejected with FA_ERR_INVALID_ARG
+ * and a message giving the size it needs.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make it before any
- * stream capture. All calls share the array: calls that may overlap on the
- * GPU (several streams or host threads) race and must be serialised by the
- * caller. In-kernel timeouts and fp16 range errors of this entry point are
- * recorded on the device but not reported. */
+ * stream capture. Only the primary context of each device is supported.
+ * All calls share the array: calls that may overlap on the GPU (several
+ * streams or host threads) race and must be serialised by the caller.
+ * In-kernel timeouts of this entry point are reported by
+ * fa_noalloc_check_status. */
 fa_status fa_forward_noalloc(const fa_params* p, const void* q, const void* k,
                              const void* v, void* o, float* lse, const float* cos,
                              const float* sin, void* stream);
+
+/* Status of fa_forward_noalloc's kernels on the current device (after the
+ * stream has been synchronised): reads and clears their status word with
+ * cudaMemcpy / cudaMemset, allocating nothing. FA_ERR_TIMEOUT when a wait
+ * ran out since the last call (that call's output is invalid), else FA_OK. */
+fa_status fa_noalloc_check_status(void);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,7 @@
 """Generate the golden attention fixtures from the reference's own oracles.
 
 Run in a container where the reference checkout is mounted (read-only is
-fine):  python tests/golden/make_golden.py /root/reference
+fine):  python tests/golden/make_golden.py <reference checkout>
 
 It imports `attention_ref` (test.py:39-93) and `torch_attention_reference`
 (verify_correctness.py:34-66) from the reference with a stub
@@ -180,4 +180,6 @@ def main(ref_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of the reference checkout>")
+    main(sys.argv[1])

@@ -10,7 +10,7 @@ import numpy as np
 
 from conftest import ROOT
 from oracle import attention_oracle as orc
-from test_zz_no_alloc import FaParams
+from fa_ctypes import FaParams
 
 LIB = os.path.join(ROOT, "flash_attn_metal_cpp_b200", "libfa_b200.so")
 HEADER = os.path.join(ROOT, "include", "fa_b200.h")
@@ -59,16 +59,36 @@ def test_workspace_size_per_path():
 
     q16 = 2 * 1000 * 8 * 128 * 2
     kv16 = 2 * 1000 * 2 * 128 * 2
+    rec = 256                                     # staging record (per-tensor range exponents)
     assert ws(0, False) == 0                      # fp16, no RoPE: zero-copy
-    assert ws(1, False) == kv16                   # bf16: V staged as fp16
-    assert ws(0, True) == q16 + kv16              # fp16 + RoPE: rotated Q, K
-    assert ws(1, True) == q16 + 2 * kv16          # bf16 + RoPE: Q, K, V
+    assert ws(1, False) == rec + kv16             # bf16: V staged as fp16
+    assert ws(0, True) == rec + q16 + kv16        # fp16 + RoPE: rotated Q, K
+    assert ws(1, True) == rec + q16 + 2 * kv16    # bf16 + RoPE: Q, K, V
     assert ws(2, True) == 0                       # fp32: CUDA-core kernel, RoPE on load
     up = lambda x: (x + 255) // 256 * 256  # noqa: E731
     q128, kv128 = 2 * 1000 * 8 * 128 * 2, 2 * 1000 * 2 * 128 * 2
-    assert ws(0, True, D=96) == up(q128) + 2 * up(kv128) + up(q128)  # padded to 128: Q, K, V and O
-    assert ws(1, False, D=40) == up(q128 // 2) + 2 * up(kv128 // 2) + up(q128 // 2)  # padded to 64
+    assert ws(0, True, D=96) == rec + up(q128) + 2 * up(kv128) + up(q128)  # padded to 128: Q, K, V and O
+    assert ws(1, False, D=40) == rec + up(q128 // 2) + 2 * up(kv128 // 2) + up(q128 // 2)  # padded to 64
     assert ws(0, True, D=160) == 0                # head dims above 128: CUDA-core kernel
+
+
+def test_wait_limit_setting():
+    """The in-kernel wait limit is a host setting (no device needed)."""
+    from fa_ctypes import load_lib
+
+    lib = load_lib()
+    assert abs(lib.fa_get_wait_limit() - 2.0) < 1e-12 or lib.fa_get_wait_limit() > 0
+    before = lib.fa_get_wait_limit()
+    try:
+        assert lib.fa_set_wait_limit(0.5) == 0
+        assert abs(lib.fa_get_wait_limit() - 0.5) < 1e-9
+        assert lib.fa_set_wait_limit(0.0) == 1 and b"wait limit" in lib.fa_last_error()
+        assert lib.fa_set_wait_limit(-1.0) == 1
+        assert lib.fa_set_wait_limit(float("nan")) == 1
+        assert abs(lib.fa_get_wait_limit() - 0.5) < 1e-9  # rejected values leave it unchanged
+        assert lib.fa_test_stall_next_launch(-1) == 1
+    finally:
+        lib.fa_set_wait_limit(before)
 
 
 def test_rope_tables_match_oracle():

@@ -44,7 +44,7 @@ CASES = [
     (1, 777, 777, 8, 2, 128, "bfloat16", False, None, True, 5e5),         # non-causal ALiBi + RoPE
     (1, 900, 900, 4, 1, 64, "bfloat16", True, (300, 0), True, 1e4),       # window + ALiBi
     (1, 300, 400, 2, 1, 40, "float32", True, (64, 16), True, None),       # CUDA-core kernel, Sq != Sk
-    (1, 256, 256, 4, 4, 96, "float16", False, (32, 32), True, None),      # CUDA-core kernel, D = 96
+    (1, 256, 256, 4, 4, 96, "float16", False, (32, 32), True, None),      # D = 96 zero-padded to 128 (tensor cores)
 ]
 
 

@@ -363,3 +363,31 @@ def test_odd_head_dims_padded_onto_tensor_cores(fa, cuda_device, D, dtype, causa
     out_h = fa.forward(q.cpu(), k.cpu(), v.cpu(), softmax_scale=1 / math.sqrt(D), is_causal=causal,
                        out_dtype="float32", **kw)
     assert np.array_equal(out_h.numpy(), out.cpu().numpy())
+
+
+def test_metal_attention_wrapper_with_data(fa, cuda_device):
+    """The package wrapper (reference __init__.py:48-89): inputs of any kind
+    converted to NumPy float16, scale defaulting to 1/sqrt(head_dim), NumPy
+    float16 output equal to the oracle within the fp16 output bar."""
+    import torch
+
+    import flash_attn_metal_cpp_b200 as pkg
+
+    rng = np.random.default_rng(8)
+    q = rng.standard_normal((2, 200, 4, 64)).astype(np.float32)
+    k = rng.standard_normal((2, 200, 2, 64)).astype(np.float32)
+    v = rng.standard_normal((2, 200, 2, 64)).astype(np.float32)
+    out = pkg.metal_attention(q, k, v, causal=True)
+    assert isinstance(out, np.ndarray) and out.dtype == np.float16 and out.shape == q.shape
+    q16, k16, v16 = (x.astype(np.float16).astype(np.float32) for x in (q, k, v))
+    ref = orc.attention_ref(q16, k16, v16, causal=True, softmax_scale=1 / math.sqrt(64))
+    d = np.abs(out.astype(np.float64) - ref)
+    assert (d <= 2e-3 + 2.0**-11 * np.abs(ref)).all(), f"max_abs={d.max():.3e}"
+    # torch tensors (CUDA or CPU) and nested lists give the same array
+    assert np.array_equal(pkg.metal_attention(*(torch.from_numpy(x).to(cuda_device) for x in (q, k, v)),
+                                              causal=True), out)
+    assert np.array_equal(pkg.metal_attention(q.tolist(), k.tolist(), v.tolist(), causal=True), out)
+    # an explicit scale is honoured
+    out2 = pkg.metal_attention(q, k, v, causal=False, softmax_scale=0.3)
+    ref2 = orc.attention_ref(q16, k16, v16, causal=False, softmax_scale=0.3)
+    assert np.abs(out2.astype(np.float64) - ref2).max() <= 2e-3 + 2.0**-11 * np.abs(ref2).max()

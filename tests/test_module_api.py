@@ -69,7 +69,16 @@ def test_forward_validation_errors(fam):
 
 
 def test_package_wrapper(fam):
+    import torch
+
     import flash_attn_metal_cpp_b200 as pkg
 
     assert callable(pkg.metal_attention)
     assert pkg.forward is fam.forward
+    # Inputs become NumPy arrays as in the reference wrapper (np.array(x)).
+    x = np.arange(24, dtype=np.float32).reshape(1, 2, 3, 4)
+    assert pkg._to_numpy(x) is x
+    assert np.array_equal(pkg._to_numpy(torch.from_numpy(x)), x)
+    assert np.array_equal(pkg._to_numpy(x.tolist()), x)
+    assert pkg._to_numpy(torch.from_numpy(x).to(torch.bfloat16)).dtype == np.float32
+    assert set(fam.get_wait_limit.__doc__.split()) & {"wait", "limit"}

@@ -162,3 +162,58 @@ def test_splitkv_plan_covers_and_balances(Sq, Sk, W, causal):
     assert max(work) <= sum(work) / W + tile_max
     if Sq >= 65536:
         assert max(work) / min(work) < 1.05
+
+
+# ------------------------------------------------- a rank leaves before the merge
+def _leaver_worker(rank, world, port, how, result_path):
+    """Rank 1 leaves before the split-KV merge barrier (it exits, or stays but
+    never arrives); rank 0 must get PeerLostError within the process group's
+    timeout instead of merging stale staging or waiting forever."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from flash_attn_metal_cpp_b200.multi_gpu import PeerLostError, merge_barrier
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    flag = torch.zeros(1)
+    merge_barrier(flag)  # a healthy step: both ranks arrive
+    if rank == 1:
+        if how == "never_arrives":
+            time.sleep(8)  # past rank 0's timeout, then leave without the barrier
+        os._exit(0)  # leave between steps, with no collective in flight
+    t0 = time.monotonic()
+    try:
+        merge_barrier(flag)
+        outcome = "no error"
+    except PeerLostError as exc:
+        outcome = "peer lost" if "split-KV merge barrier failed" in str(exc) else f"wrong text: {exc}"
+    except Exception as exc:  # noqa: BLE001
+        outcome = f"other error: {type(exc).__name__}: {exc}"
+    with open(result_path, "w") as f:
+        f.write(f"{outcome}\n{time.monotonic() - t0:.2f}\n")
+    os._exit(0)  # the group is broken: skip destroy_process_group
+
+
+@pytest.mark.parametrize("how", ["exits", "never_arrives"])
+def test_rank_leaving_before_merge_raises(tmp_path, how):
+    import torch.multiprocessing as mp
+
+    path = str(tmp_path / "result.txt")
+    ctx = mp.start_processes(_leaver_worker, args=(2, _free_port(), how, path), nprocs=2, join=False,
+                             start_method="spawn")
+    import time
+
+    deadline = time.monotonic() + 60
+    while not ctx.join(timeout=5) and time.monotonic() < deadline:
+        pass  # join() returns after each process that ends; wait for both
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    outcome, elapsed = open(path).read().split("\n")[:2]
+    assert outcome == "peer lost", outcome
+    assert float(elapsed) < 30.0

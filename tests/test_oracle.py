@@ -25,6 +25,23 @@ def test_oracle_matches_reference_fixture(name):
     assert np.abs(got - ref).max() <= 1e-5 * scale + 1e-7, name
 
 
+@pytest.mark.parametrize("name", golden_names())
+def test_torch_cpu_baseline_matches_reference_fixture(name):
+    """The PyTorch-CPU restatement timed as the CPU baseline computes what the
+    reference's attention_ref computed for the fixtures."""
+    import torch
+
+    from oracle.torch_cpu_reference import attention_ref_torch
+
+    g = load_golden(name)
+    m = g["meta"]
+    q, k, v = (torch.from_numpy(g[x]) for x in ("q", "k", "v"))
+    got = attention_ref_torch(q, k, v, causal=m["causal"], softmax_scale=m["scale"],
+                              rope_theta=m.get("rope_theta")).numpy()
+    scale = float(np.abs(g["out"]).max())
+    assert np.abs(got - g["out"]).max() <= 1e-5 * scale + 1e-7, name
+
+
 @pytest.mark.parametrize("name", ["v1_causal_s256_h8_d64", "v2_full_s128_h8_d64"])
 def test_fp16_cast_oracle_matches_verify_correctness(name):
     """torch_attention_reference (verify_correctness.py:34-66) returns fp16."""

@@ -1,6 +1,5 @@
-"""The C layout of fa_params (include/fa_b200.h) against the ctypes mirrors
-that callers use: the one in the GPU test of the allocation-free entry point
-and the one INTEGRATION.md gives as the binding to copy. A drifted mirror
+"""The C layout of fa_params (include/fa_b200.h) against the ctypes mirror
+the tests bind the library with (tests/fa_ctypes.py). A drifted mirror
 would make fa_params_init write past the end of the Python structure, so the
 size and every field offset must agree. Compiles a small C program with gcc;
 runs on CPU."""
@@ -8,7 +7,6 @@ from __future__ import annotations
 
 import ctypes
 import os
-import re
 import shutil
 import subprocess
 
@@ -46,18 +44,7 @@ def _check(struct_cls, layout):
         assert getattr(struct_cls, f).offset == layout[f], f
 
 
-def test_gpu_test_mirror_matches_header(c_layout):
-    import importlib.util
-    spec = importlib.util.spec_from_file_location("_noalloc_test", os.path.join(ROOT, "tests", "test_zz_no_alloc.py"))
-    mod = importlib.util.module_from_spec(spec)
-    spec.loader.exec_module(mod)
-    _check(mod.FaParams, c_layout)
+def test_ctypes_mirror_matches_header(c_layout):
+    from fa_ctypes import FaParams
 
-
-def test_integration_binding_matches_header(c_layout):
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    m = re.search(r"class fa_params\(ctypes\.Structure\):.*?\]\n", text, re.S)
-    assert m, "INTEGRATION.md no longer shows the fa_params binding"
-    ns = {"ctypes": ctypes}
-    exec(m.group(0), ns)  # the documented class definition, as a user would paste it
-    _check(ns["fa_params"], c_layout)
+    _check(FaParams, c_layout)
