@@ -351,7 +351,7 @@ def test_odd_head_dims_padded_onto_tensor_cores(fa, cuda_device, D, dtype, causa
                           return_lse=True, **kw)
     torch.cuda.synchronize()
     fa.check_status()
-    assert fa.launch_count() - n0 >= 5, "expected the padded tensor-core path (staging + kernel + copy-out)"
+    assert fa.launch_count() - n0 >= 4, "expected the padded tensor-core path (staging, range fixup, kernel, copy-out)"
     qn, kn, vn = (x.float().cpu().numpy() for x in (q, k, v))
     if kw:
         ref, ref_l = orc.attention_with_rope(qn, kn, vn, causal, 1 / math.sqrt(D), cos=cs, sin=sn, return_lse=True)
