@@ -33,6 +33,7 @@ NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-r
 CU_SOURCES = [
     "fa_api.cu",
     "fa_aux.cu",
+    "fa_host.cu",
     "fa_fwd_simt.cu",
     "fa_fwd_sm100.cu",
     "fa_fwd_sm100_d64_causal.cu",
@@ -40,7 +41,7 @@ CU_SOURCES = [
     "fa_fwd_sm100_d128_causal.cu",
     "fa_fwd_sm100_d128_full.cu",
 ]
-HEADERS = ["fa_internal.h", "fa_ptx.cuh", "fa_fwd_sm100.cuh"]
+HEADERS = ["fa_internal.h", "fa_ptx.cuh", "fa_fwd_sm100.cuh", "fa_host.h"]
 
 
 def _mtime(path: str) -> float:

@@ -114,6 +114,27 @@ py::dtype numpy_dtype_of(int code) {
   return py::dtype::from_args(bf16_numpy_dtype());
 }
 
+// A C-ordered NumPy array in pinned host memory from the library's pool (the
+// device-to-host copy of the result then runs by DMA at full link speed);
+// the array owns the buffer and returns it to the pool when it dies. Falls
+// back to ordinary memory when no pinned memory is left.
+py::array pinned_array(const py::dtype& dt, std::vector<int64_t> shape) {
+  size_t n = 1;
+  for (int64_t d : shape) n *= (size_t)d;
+  const size_t bytes = n * (size_t)dt.itemsize();
+  std::vector<py::ssize_t> sh(shape.begin(), shape.end());
+  void* buf = nullptr;
+  if (bytes == 0 || fa_host_alloc(bytes, &buf) != FA_OK) return py::array(dt, sh);
+  py::capsule owner(buf, [](void* p) { fa_host_free(p); });
+  std::vector<py::ssize_t> strides(sh.size());
+  py::ssize_t st = dt.itemsize();
+  for (size_t i = sh.size(); i-- > 0;) {
+    strides[i] = st;
+    st *= sh[i];
+  }
+  return py::array(dt, sh, strides, buf, owner);
+}
+
 py::object forward_numpy(py::object Q, py::object K, py::object V, float scale, bool causal,
                          float dropout_p, py::object alibi, py::object window, py::object cos,
                          py::object sin, int out_code, float rope_theta, bool return_lse) {
@@ -152,13 +173,12 @@ py::object forward_numpy(py::object Q, py::object K, py::object V, float scale, 
     cp = static_cast<const float*>(c_arr.data());
     sp = static_cast<const float*>(s_arr.data());
   }
-  py::array out(numpy_dtype_of(oc), std::vector<py::ssize_t>{(py::ssize_t)qs[0], (py::ssize_t)qs[1],
-                                                              (py::ssize_t)qs[2], (py::ssize_t)qs[3]});
-  py::array_t<float> lse;
+  py::array out = pinned_array(numpy_dtype_of(oc), {qs[0], qs[1], qs[2], qs[3]});
+  py::array lse;
   float* lp = nullptr;
   if (return_lse) {
-    lse = py::array_t<float>(std::vector<py::ssize_t>{(py::ssize_t)qs[0], (py::ssize_t)qs[2], (py::ssize_t)qs[1]});
-    lp = lse.mutable_data();
+    lse = pinned_array(py::dtype("float32"), {qs[0], qs[2], qs[1]});
+    lp = static_cast<float*>(lse.mutable_data());
   }
   fa_status st;
   {
@@ -198,6 +218,17 @@ py::object check_out(py::object out, const py::tuple& shape, int oc, bool cuda) 
   return out;
 }
 
+// A CPU torch tensor over pinned_array memory (bf16 through a 16-bit view,
+// since NumPy has no bfloat16 that torch.from_numpy accepts).
+py::object pinned_tensor(std::vector<int64_t> shape, int code) {
+  py::module_ torch = py::module_::import("torch");
+  const py::dtype nd = code == FA_F32 ? py::dtype("float32") : (code == FA_F16 ? py::dtype("float16")
+                                                                                : py::dtype("int16"));
+  py::object t = torch.attr("from_numpy")(pinned_array(nd, std::move(shape)));
+  if (code == FA_BF16) t = t.attr("view")(torch.attr("bfloat16"));
+  return t;
+}
+
 py::object forward_torch(py::object Q, py::object K, py::object V, float scale, bool causal,
                          float dropout_p, py::object alibi, py::object window, py::object cos,
                          py::object sin, int out_code, float rope_theta, bool return_lse,
@@ -232,12 +263,13 @@ py::object forward_torch(py::object Q, py::object K, py::object V, float scale, 
   if (!cuda) {
     // CPU tensors: host path (contiguous), like the NumPy route.
     py::object q = Q.attr("contiguous")(), k = K.attr("contiguous")(), v = V.attr("contiguous")();
-    py::object out = out_arg.is_none() ? torch.attr("empty")(shape, py::arg("dtype") = torch_dtype_of(oc))
+    // Results in the library's pinned memory: copied back by DMA.
+    py::object out = out_arg.is_none() ? pinned_tensor({qs[0], qs[1], qs[2], qs[3]}, oc)
                                        : check_out(out_arg, shape, oc, false);
     py::object lse = py::none();
     float* lp = nullptr;
     if (return_lse) {
-      lse = torch.attr("empty")(py::make_tuple(qs[0], qs[2], qs[1]), py::arg("dtype") = torch.attr("float32"));
+      lse = pinned_tensor({qs[0], qs[2], qs[1]}, FA_F32);
       lp = reinterpret_cast<float*>(lse.attr("data_ptr")().cast<uintptr_t>());
     }
     py::object ct = py::none(), stt = py::none();

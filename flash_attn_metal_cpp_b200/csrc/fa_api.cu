@@ -12,6 +12,7 @@
 // other head dims) runs on the CUDA-core kernel (fa_fwd_simt.cu). There is
 // no CPU path: without a CUDA device every entry point returns an error.
 #include "../../include/fa_b200.h"
+#include "fa_host.h"
 #include "fa_internal.h"
 #include "fa_ptx.cuh"
 
@@ -140,6 +141,7 @@ struct DeviceState {
   int device = -1;
   bool ready = false;
   unsigned* status = nullptr;       // in-kernel status word
+  void* status_host = nullptr;      // pinned copy of it, read back by the host-pointer path
   cudaStream_t host_stream = nullptr;   // host-pointer path: compute
   cudaStream_t h2d_stream = nullptr;    // host-pointer path: copies in
   cudaStream_t d2h_stream = nullptr;    // host-pointer path: copies out
@@ -201,6 +203,7 @@ fa_status device_state(DeviceState** out) {
                                           "' is not sm_100 (B200); this library is built for sm_100a only");
     FA_CUDA(cudaMalloc(&ds->status, sizeof(unsigned)));
     FA_CUDA(cudaMemset(ds->status, 0, sizeof(unsigned)));
+    ds->status_host = pinned_get(sizeof(unsigned));  // NULL: the host path reads the word synchronously
     FA_CUDA(cudaStreamCreateWithFlags(&ds->host_stream, cudaStreamNonBlocking));
     FA_CUDA(cudaStreamCreateWithFlags(&ds->h2d_stream, cudaStreamNonBlocking));
     FA_CUDA(cudaStreamCreateWithFlags(&ds->d2h_stream, cudaStreamNonBlocking));
@@ -880,18 +883,14 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
   const size_t o_bytes = (size_t)a.B * a.Sq * a.Hq * a.D * out_sz;
   const size_t lse_bytes = (size_t)a.B * a.Hq * a.Sq * sizeof(float);
   const size_t tab_bytes = (size_t)(a.Sq > a.Sk ? a.Sq : a.Sk) * (a.D / 2) * sizeof(float);
-  const bool tables = p->has_rotary && cos && sin;
+  const bool tables = p->has_rotary && cos && sin && tab_bytes > 0;
   cudaStream_t s = ds->host_stream;
   Lease dq(&ds->pool, q_bytes), dk(&ds->pool, k_bytes), dv(&ds->pool, k_bytes), dout(&ds->pool, o_bytes),
       dl(&ds->pool, lse ? lse_bytes : 0), dc(&ds->pool, tables ? tab_bytes : 0),
       dsn(&ds->pool, tables ? tab_bytes : 0), dws(&ds->pool, pl.ws_bytes);
   if ((q_bytes && !dq.p) || (k_bytes && (!dk.p || !dv.p)) || (o_bytes && !dout.p) || (lse && lse_bytes && !dl.p) ||
-      (tables && tab_bytes && (!dc.p || !dsn.p)) || (pl.ws_bytes && !dws.p))
+      (tables && (!dc.p || !dsn.p)) || (pl.ws_bytes && !dws.p))
     return fail(FA_ERR_CUDA, "device allocation failed");
-  if (tables && tab_bytes) {
-    FA_CUDA(cudaMemcpyAsync(dc.p, cos, tab_bytes, cudaMemcpyHostToDevice, s));
-    FA_CUDA(cudaMemcpyAsync(dsn.p, sin, tab_bytes, cudaMemcpyHostToDevice, s));
-  }
   const float* tc = tables ? static_cast<const float*>(dc.p) : nullptr;
   const float* tsn = tables ? static_cast<const float*>(dsn.p) : nullptr;
   // ALiBi slopes arrive in host memory here: stage them next to the tensors.
@@ -930,25 +929,122 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
       for (int i = n_blk - 1; i >= 0; --i)
         chunks.push_back({b, i * rows, std::min(a.Sq, (i + 1) * rows), i == n_blk - 1});
   }
-  if (chunks.size() <= 1 || q_bytes == 0 || k_bytes == 0) {
-    // One piece: copy in, run, copy out on one stream.
-    if (q_bytes) FA_CUDA(cudaMemcpyAsync(dq.p, q, q_bytes, cudaMemcpyHostToDevice, s));
-    if (k_bytes) {
-      FA_CUDA(cudaMemcpyAsync(dk.p, k, k_bytes, cudaMemcpyHostToDevice, s));
-      FA_CUDA(cudaMemcpyAsync(dv.p, v, k_bytes, cudaMemcpyHostToDevice, s));
+  const bool one_piece = chunks.size() <= 1 || q_bytes == 0 || k_bytes == 0;
+  if (one_piece) chunks.assign(1, Chunk{0, 0, a.Sq, true});
+
+  // Host memory. Pinned (page-locked) buffers are DMA'd directly. Pageable
+  // inputs are first copied into pinned staging by the copy workers, in the
+  // order the copies below are issued, each DMA waiting only for its own
+  // bytes; pageable outputs are DMA'd into pinned staging and copied out at
+  // the end. (The driver's own route for pageable memory is several times
+  // slower than the link.)
+  struct Src { const void* user; size_t bytes; bool pageable; size_t stage_off; };
+  Src srcs[5] = {{q, q_bytes, false, 0}, {k, k_bytes, false, 0}, {v, k_bytes, false, 0},
+                 {cos, tables ? tab_bytes : 0, false, 0}, {sin, tables ? tab_bytes : 0, false, 0}};
+  size_t stage_in = 0;
+  for (Src& x : srcs)
+    if (x.bytes && !host_is_pinned(x.user)) {
+      x.pageable = true;
+      x.stage_off = stage_in;
+      stage_in += (x.bytes + 255) & ~size_t(255);
     }
+  const bool o_pg = o_bytes && !host_is_pinned(o);
+  const bool l_pg = lse && lse_bytes && !host_is_pinned(lse);
+  const size_t o_stage = o_pg ? ((o_bytes + 255) & ~size_t(255)) : 0;
+  const size_t stage_out = o_stage + (l_pg ? lse_bytes : 0);
+  struct PinnedLease {
+    void* p = nullptr;
+    explicit PinnedLease(size_t n) : p(n ? pinned_get(n) : nullptr) {}
+    ~PinnedLease() { pinned_put(p); }
+  } pin_in(stage_in), pin_out(stage_out);
+  if (stage_in && !pin_in.p)  // no pinned memory to spare: the driver's pageable route
+    for (Src& x : srcs) x.pageable = false;
+  char* st_in = static_cast<char*>(pin_in.p);
+  char* st_out = static_cast<char*>(pin_out.p);
+  void* o_dst = (o_pg && st_out) ? st_out : o;
+  float* l_dst = (l_pg && st_out) ? reinterpret_cast<float*>(st_out + o_stage) : lse;
+
+  // Every host->device copy in issue order: tables first, then per chunk the
+  // batch's K and V (with its first block) and the block's Q rows.
+  struct H2D { int chunk; void* dst; int src; size_t off, bytes; int region; };
+  std::vector<H2D> h2d;
+  if (tables) {
+    h2d.push_back({-1, dc.p, 3, 0, tab_bytes, -1});
+    h2d.push_back({-1, dsn.p, 4, 0, tab_bytes, -1});
+  }
+  const size_t q_row = (size_t)a.Hq * a.D, k_row = (size_t)a.Hk * a.D;  // elements per sequence row
+  for (size_t c = 0; c < chunks.size(); ++c) {
+    const Chunk& ch = chunks[c];
+    if (one_piece) {
+      if (k_bytes) {
+        h2d.push_back({0, dk.p, 1, 0, k_bytes, -1});
+        h2d.push_back({0, dv.p, 2, 0, k_bytes, -1});
+      }
+      if (q_bytes) h2d.push_back({0, dq.p, 0, 0, q_bytes, -1});
+      continue;
+    }
+    const size_t k_off = (size_t)ch.b * a.Sk * k_row * in_sz;
+    const size_t q_off = ((size_t)ch.b * a.Sq + ch.r0) * q_row * in_sz;
+    if (ch.kv_first) {
+      h2d.push_back({(int)c, static_cast<char*>(dk.p) + k_off, 1, k_off, (size_t)a.Sk * k_row * in_sz, -1});
+      h2d.push_back({(int)c, static_cast<char*>(dv.p) + k_off, 2, k_off, (size_t)a.Sk * k_row * in_sz, -1});
+    }
+    h2d.push_back({(int)c, static_cast<char*>(dq.p) + q_off, 0, q_off, (size_t)(ch.r1 - ch.r0) * q_row * in_sz, -1});
+  }
+  std::vector<CopyRegion> regions;
+  for (H2D& h : h2d) {
+    const Src& x = srcs[h.src];
+    if (!x.pageable) continue;
+    h.region = (int)regions.size();
+    regions.push_back({st_in + x.stage_off + h.off, static_cast<const char*>(x.user) + h.off, h.bytes});
+  }
+  Stager stager;
+  if (!regions.empty()) stager.start(std::move(regions));
+  auto issue_h2d = [&](const H2D& h, cudaStream_t stream) -> cudaError_t {
+    const Src& x = srcs[h.src];
+    const char* from = static_cast<const char*>(x.user) + h.off;
+    if (h.region >= 0) {
+      stager.wait((size_t)h.region);
+      from = st_in + x.stage_off + h.off;
+    }
+    return cudaMemcpyAsync(h.dst, from, h.bytes, cudaMemcpyHostToDevice, stream);
+  };
+  // The in-kernel status word is read back with the results (no extra sync).
+  unsigned* status_host = static_cast<unsigned*>(ds->status_host);
+  auto finish_status = [&]() -> fa_status {
+    if (status_host == nullptr || *status_host != 0) return fa_check_device_status();
+    return FA_OK;
+  };
+  // Pageable outputs: copy the staged results out with the workers (the
+  // same stager: start() ends the input job first, one job at a time).
+  auto copy_out = [&]() {
+    std::vector<CopyRegion> outs;
+    if (o_pg && st_out) outs.push_back({o, st_out, o_bytes});
+    if (l_pg && st_out) outs.push_back({lse, st_out + o_stage, lse_bytes});
+    stager.finish();
+    if (outs.empty()) return;
+    stager.start(std::move(outs));
+    stager.finish();
+  };
+
+  if (one_piece) {
+    // One piece: copy in, run, copy out on one stream.
+    for (const H2D& h : h2d) FA_CUDA(issue_h2d(h, s));
     pl.a.o = dout.p;
     pl.a.lse = static_cast<float*>(dl.p);
     st = run(pl, dq.p ? dq.p : (const void*)1, dk.p ? dk.p : (const void*)1, dv.p ? dv.p : (const void*)1, tc,
              tsn, dws.p, pl.ws_bytes, s, ds, ds->status);
     if (st != FA_OK) {
+      stager.finish();
       cudaStreamSynchronize(s);
       return st;
     }
-    if (o_bytes) FA_CUDA(cudaMemcpyAsync(o, dout.p, o_bytes, cudaMemcpyDeviceToHost, s));
-    if (lse && lse_bytes) FA_CUDA(cudaMemcpyAsync(lse, dl.p, lse_bytes, cudaMemcpyDeviceToHost, s));
+    if (o_bytes) FA_CUDA(cudaMemcpyAsync(o_dst, dout.p, o_bytes, cudaMemcpyDeviceToHost, s));
+    if (lse && lse_bytes) FA_CUDA(cudaMemcpyAsync(l_dst, dl.p, lse_bytes, cudaMemcpyDeviceToHost, s));
+    if (status_host) FA_CUDA(cudaMemcpyAsync(status_host, ds->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s));
     FA_CUDA(cudaStreamSynchronize(s));
-    return fa_check_device_status();
+    copy_out();
+    return finish_status();
   }
 
   cudaStream_t s_in = ds->h2d_stream, s_out = ds->d2h_stream;
@@ -957,7 +1053,7 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
     cudaStreamSynchronize(s);
     cudaStreamSynchronize(s_out);
   };
-  // The copies of the tables above were queued on `s`; the copy stream waits for them too.
+  // The ALiBi copy above was queued on `s`; the copy stream waits for it too.
   cudaEvent_t ev_tab;
   FA_CUDA(cudaEventCreateWithFlags(&ev_tab, cudaEventDisableTiming));
   FA_CUDA(cudaEventRecord(ev_tab, s));
@@ -974,23 +1070,17 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
       cudaEventDestroy(ev_done[c]);
     }
   };
-  const size_t q_row = (size_t)a.Hq * a.D, k_row = (size_t)a.Hk * a.D;  // elements per sequence row
   st = FA_OK;
+  size_t hi = 0;  // next entry of h2d
   for (size_t c = 0; c < chunks.size() && st == FA_OK; ++c) {
     const Chunk& ch = chunks[c];
     const size_t k_off = (size_t)ch.b * a.Sk * k_row;                  // elements
     const size_t q_off = ((size_t)ch.b * a.Sq + ch.r0) * q_row;
     const size_t nrows = (size_t)(ch.r1 - ch.r0);
-    // copy in: the batch's K and V with its first block, then the block's Q rows
+    // copy in: the tables (before the first chunk), the batch's K and V with
+    // its first block, then the block's Q rows
     cudaError_t e = cudaSuccess;
-    if (ch.kv_first)
-      for (int m = 0; m < 2 && e == cudaSuccess; ++m)
-        e = cudaMemcpyAsync(static_cast<char*>(m ? dv.p : dk.p) + k_off * in_sz,
-                            static_cast<const char*>(m ? v : k) + k_off * in_sz, (size_t)a.Sk * k_row * in_sz,
-                            cudaMemcpyHostToDevice, s_in);
-    if (e == cudaSuccess)
-      e = cudaMemcpyAsync(static_cast<char*>(dq.p) + q_off * in_sz, static_cast<const char*>(q) + q_off * in_sz,
-                          nrows * q_row * in_sz, cudaMemcpyHostToDevice, s_in);
+    for (; hi < h2d.size() && h2d[hi].chunk <= (int)c && e == cudaSuccess; ++hi) e = issue_h2d(h2d[hi], s_in);
     if (e == cudaSuccess) e = cudaEventRecord(ev_in[c], s_in);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ev_in[c], 0);
     if (e != cudaSuccess) {
@@ -1014,23 +1104,37 @@ fa_status fa_forward_host(const fa_params* p, const void* q, const void* k, cons
     if (e == cudaSuccess) e = cudaStreamWaitEvent(s_out, ev_done[c], 0);
     // copy out: the block's O rows, and its LSE columns [r0, r1) of every head
     if (e == cudaSuccess)
-      e = cudaMemcpyAsync(static_cast<char*>(o) + q_off * out_sz, static_cast<const char*>(dout.p) + q_off * out_sz,
+      e = cudaMemcpyAsync(static_cast<char*>(o_dst) + q_off * out_sz, static_cast<const char*>(dout.p) + q_off * out_sz,
                           nrows * q_row * out_sz, cudaMemcpyDeviceToHost, s_out);
     if (e == cudaSuccess && lse) {
       const size_t l_off = (size_t)ch.b * a.Hq * a.Sq + ch.r0;
-      e = cudaMemcpy2DAsync(lse + l_off, (size_t)a.Sq * sizeof(float), static_cast<const float*>(dl.p) + l_off,
+      e = cudaMemcpy2DAsync(l_dst + l_off, (size_t)a.Sq * sizeof(float), static_cast<const float*>(dl.p) + l_off,
                             (size_t)a.Sq * sizeof(float), nrows * sizeof(float), (size_t)a.Hq,
                             cudaMemcpyDeviceToHost, s_out);
     }
     if (e != cudaSuccess) st = cuda_fail(e, "chunk copy out");
   }
+  if (st == FA_OK && status_host) {
+    cudaError_t e = cudaMemcpyAsync(status_host, ds->status, sizeof(unsigned), cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) st = cuda_fail(e, "status read-back");
+  }
+  stager.finish();
   sync_all();
   destroy_events();
   if (st != FA_OK) return st;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "pipelined host path");
-  return fa_check_device_status();
+  copy_out();
+  return finish_status();
 }
+
+fa_status fa_host_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(FA_ERR_INVALID_ARG, "bad fa_host_alloc arguments");
+  *ptr = pinned_get(bytes);
+  return *ptr ? FA_OK : fail(FA_ERR_CUDA, "pinned host allocation failed");
+}
+
+void fa_host_free(void* ptr) { pinned_put(ptr); }
 
 fa_status fa_rope_tables(float* cos_out, float* sin_out, uint32_t rows, uint32_t head_dim, float theta) {
   if (!cos_out || !sin_out || head_dim == 0 || head_dim % 2 || !(theta > 0.f))
@@ -1072,6 +1176,7 @@ fa_status fa_pool_clear(void) {
   ds->rope.clear();
   for (auto& kv : ds->ws) cudaFree(kv.second.first);
   ds->ws.clear();
+  pinned_release_cached();
   return FA_OK;
 }
 

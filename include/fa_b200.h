@@ -150,10 +150,25 @@ fa_status fa_forward(const fa_params* p, const void* q, const void* k,
 
 /* Whole-call path on HOST pointers: copies Q/K/V (and tables) to device
  * buffers from the library pool, runs fa_forward, copies O (and LSE when
- * non-NULL) back and synchronises, like FlashAttentionForward::execute. */
+ * non-NULL) back and synchronises, like FlashAttentionForward::execute.
+ * Large calls are pipelined over query-row blocks (copy in, compute, copy
+ * out on three streams). Host buffers may be pinned or pageable: pageable
+ * inputs are copied into pinned staging by a few worker threads (set their
+ * number with the FA_HOST_COPY_THREADS environment variable) piece by
+ * piece, each piece DMA'd as soon as it is staged; pageable outputs are
+ * staged the same way on the way back. */
 fa_status fa_forward_host(const fa_params* p, const void* q, const void* k,
                           const void* v, void* o, float* lse, const float* cos,
                           const float* sin);
+
+/* Pinned (page-locked) host memory from the library's pool (no counterpart
+ * in the reference, whose Metal buffers are shared with the host). Outputs
+ * the caller lets the library allocate (the Python module's NumPy results)
+ * live here, so fa_forward_host copies them back by DMA at full link speed;
+ * fa_host_free returns a buffer to the pool (freed unused buffers beyond a
+ * few GB go back to the system; fa_pool_clear releases the rest). */
+fa_status fa_host_alloc(size_t bytes, void** ptr);
+void fa_host_free(void* ptr);
 
 /* Split-KV partial: attention of every query row over the keys in
  * [kv_begin, kv_end) only (after the causal mask). Writes the row-normalised

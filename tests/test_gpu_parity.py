@@ -391,3 +391,41 @@ def test_metal_attention_wrapper_with_data(fa, cuda_device):
     out2 = pkg.metal_attention(q, k, v, causal=False, softmax_scale=0.3)
     ref2 = orc.attention_ref(q16, k16, v16, causal=False, softmax_scale=0.3)
     assert np.abs(out2.astype(np.float64) - ref2).max() <= 2e-3 + 2.0**-11 * np.abs(ref2).max()
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("shape", [(2, 300, 4, 2, 64), (2, 5000, 8, 2, 128)])
+def test_host_path_pageable_and_pinned_buffers(fa, cuda_device, shape):
+    """fa_forward_host with every mix of pageable and pinned host buffers
+    (inputs staged by the copy workers, outputs staged on the way back), the
+    one-piece and the pipelined path: always the device path's result."""
+    import ctypes
+
+    import torch
+
+    from fa_ctypes import FA_F16, FA_F32, load_lib, make_params
+
+    B, S, Hq, Hk, D = shape
+    q, k, v = _inputs((B, S, Hq, D), (B, S, Hk, D), torch.float16, seed=S)
+    ref, ref_lse = fa.forward(q, k, v, softmax_scale=0.1, is_causal=True, out_dtype="float32", return_lse=True)
+    ref, ref_lse = ref.cpu().numpy(), ref_lse.cpu().numpy()
+    lib = load_lib()
+    lib.fa_forward_host.argtypes = [ctypes.c_void_p] * 8
+    lib.fa_forward_host.restype = ctypes.c_int
+    p = make_params(lib, B, S, S, Hq, Hk, D, True, FA_F16, FA_F32, scale=0.1)
+    for pin_in in (False, True):
+        for pin_out in (False, True):
+            ins = [x.cpu() for x in (q, k, v)]
+            if pin_in:
+                ins = [x.pin_memory() for x in ins]
+            else:
+                ins = [torch.from_numpy(x.numpy().copy()) for x in ins]  # ordinary (pageable) memory
+            o = torch.full((B, S, Hq, D), float("nan"))
+            lse = torch.full((B, Hq, S), float("nan"))
+            if pin_out:
+                o, lse = o.pin_memory(), lse.pin_memory()
+            st = lib.fa_forward_host(ctypes.addressof(p), *(x.data_ptr() for x in ins), o.data_ptr(), lse.data_ptr(),
+                                     None, None)
+            assert st == 0, lib.fa_last_error()
+            assert np.array_equal(o.numpy(), ref), f"pinned in {pin_in} out {pin_out}"
+            assert np.array_equal(lse.numpy(), ref_lse)
