@@ -14,6 +14,8 @@
 #include "fa_internal.h"
 #include "fa_ptx.cuh"
 
+#include <algorithm>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -100,22 +102,12 @@ __device__ __forceinline__ float stage_value(const StageJob& jb, int b, int s, i
   return ld_f<T>(src + col);
 }
 
-// Work items of job j: 8-column chunks (16 with RoPE: 8 of each half) when
-// VEC, single elements of the Dp-wide output row otherwise.
-template <bool VEC>
-__device__ __forceinline__ long long job_items(const StageJob& jb) {
-  const long long rows = (long long)jb.B * jb.S * jb.H;
-  if (!VEC) return rows * jb.Dp;
-  return rows * (jb.cs != nullptr ? jb.D / 16 : jb.D / 8);
-}
-
 // Block-wide maximum of `v` (non-negative); the result is valid in thread 0.
 __device__ __forceinline__ float block_max(float v) {
   __shared__ float part[32];
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
   const int w = threadIdx.x >> 5;
-  __syncthreads();
   if ((threadIdx.x & 31) == 0) part[w] = v;
   __syncthreads();
   if (threadIdx.x == 0)
@@ -123,80 +115,96 @@ __device__ __forceinline__ float block_max(float v) {
   return v;
 }
 
-// Staging pass over every job of the batch (one launch). VEC: each thread
-// converts 8 consecutive columns (and, with RoPE, the 8 partner columns of
-// the other half) with 16-byte loads and stores; requires Dp == D,
-// D % 16 == 0 with tables (D % 8 == 0 without) and 16-byte aligned rows.
-// Otherwise one thread per output element. Values are written unscaled; a
-// block whose largest magnitude exceeds the fp16 range records it in
-// rec->amax_bits (the fixup kernel then rewrites that tensor).
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(256) stage_kernel(const StageBatch bt) {
-  // Work items of the jobs, back to back: job 0 ends at e1, job 1 at e2.
-  const long long e1 = bt.n > 0 ? job_items<VEC>(bt.job[0]) : 0;
-  const long long e2 = e1 + (bt.n > 1 ? job_items<VEC>(bt.job[1]) : 0);
-  const long long total = e2 + (bt.n > 2 ? job_items<VEC>(bt.job[2]) : 0);
-  float am0 = 0.f, am1 = 0.f, am2 = 0.f;  // largest magnitude per job
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const int j = idx < e1 ? 0 : (idx < e2 ? 1 : 2);
-    const StageJob& jb = bt.job[j];
-    const long long li = idx - (j == 0 ? 0 : (j == 1 ? e1 : e2));
-    float m;
-    if constexpr (VEC) {
-      const bool rope = jb.cs != nullptr;
-      const int chunks = rope ? jb.D / 16 : jb.D / 8;
-      const long long rowi = li / chunks;
-      const int ch = (int)(li - rowi * chunks);
-      const int h = (int)(rowi % jb.H);
-      const long long bs = rowi / jb.H;
-      const int s = (int)(bs % jb.S);
-      const int b = (int)(bs / jb.S);
-      const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h * jb.sh;
-      __half* dst = jb.y + (((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.D;
-      if (rope) {
-        const int half = jb.D / 2;
-        const int c0 = ch * 8;
-        float a[8], bb[8];
-        load8<T>(src + c0, a);
-        load8<T>(src + c0 + half, bb);
-        const float4* cp = reinterpret_cast<const float4*>(jb.cs + (int64_t)s * half + c0);
-        const float4* sp = reinterpret_cast<const float4*>(jb.sn + (int64_t)s * half + c0);
-        const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
-        const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
-        const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
-        float ra[8], rb[8];
-        rope_rotate8(a, bb, cv, sv, ra, rb);
-        m = fmaxf(store8_half(dst + c0, ra), store8_half(dst + c0 + half, rb));
-      } else {
-        float a[8];
-        load8<T>(src + ch * 8, a);
-        m = store8_half(dst + ch * 8, a);
-      }
+// Records a block's largest magnitude of job `slot` when it is beyond the
+// fp16 range (only those matter to the fixup; in-range blocks skip the atomic).
+__device__ __forceinline__ void record_amax(RangeRec* rec, int slot, float amax) {
+  const float m = block_max(amax > kHalfMax ? amax : 0.f);
+  if (threadIdx.x == 0 && m > kHalfMax) atomicMax(&rec->amax_bits[slot], __float_as_uint(m));
+}
+
+// The job of this block: blocks [blk_end[j-1], blk_end[j]) stage job j.
+__device__ __forceinline__ int block_job(const StageBatch& bt, int& first_block, int& n_blocks) {
+  const int b = blockIdx.x;
+  const int j = b < bt.blk_end[0] ? 0 : (b < bt.blk_end[1] ? 1 : 2);
+  first_block = j == 0 ? 0 : bt.blk_end[j - 1];
+  n_blocks = bt.blk_end[j] - first_block;
+  return j;
+}
+
+// Staging pass, vectorised: each thread converts 8 consecutive columns (and,
+// with RoPE, the 8 partner columns of the other half) of one (b, s, h) row
+// with 16-byte loads and stores. Requires Dp == D, D % 16 == 0 with tables
+// (D % 8 == 0 without), 16-byte aligned rows and fewer than 2^31 chunks per
+// job (checked on the host). Each block works on one job, so the job's
+// fields sit in registers and the RoPE branch is uniform. Values are
+// written unscaled; a block whose largest magnitude exceeds the fp16 range
+// records it in rec->amax_bits (the fixup kernel then rewrites that tensor).
+template <typename T>
+__global__ void __launch_bounds__(256) stage_vec_kernel(const StageBatch bt) {
+  int first_block, n_blocks;
+  const int j = block_job(bt, first_block, n_blocks);
+  const StageJob jb = bt.job[j];
+  const bool rope = jb.cs != nullptr;
+  const int half = jb.D / 2;
+  const unsigned chunks = rope ? (unsigned)jb.D / 16 : (unsigned)jb.D / 8;  // 4, 8 or 16
+  const unsigned shift = __ffs(chunks) - 1;
+  const unsigned rows = (unsigned)jb.B * jb.S * jb.H;
+  const unsigned items = rows << shift;
+  float amax = 0.f;
+  for (unsigned li = (blockIdx.x - first_block) * blockDim.x + threadIdx.x; li < items;
+       li += (unsigned)n_blocks * blockDim.x) {
+    const unsigned rowi = li >> shift;
+    const int ch = (int)(li & (chunks - 1));
+    const unsigned bs = rowi / (unsigned)jb.H;
+    const int h = (int)(rowi - bs * (unsigned)jb.H);
+    const unsigned b = bs / (unsigned)jb.S;
+    const int s = (int)(bs - b * (unsigned)jb.S);
+    const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h * jb.sh;
+    __half* dst = jb.y + (((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.D;
+    if (rope) {
+      const int c0 = ch * 8;
+      float a[8], bb[8];
+      load8<T>(src + c0, a);
+      load8<T>(src + c0 + half, bb);
+      const float4* cp = reinterpret_cast<const float4*>(jb.cs + (int64_t)s * half + c0);
+      const float4* sp = reinterpret_cast<const float4*>(jb.sn + (int64_t)s * half + c0);
+      const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
+      const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+      const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
+      float ra[8], rb[8];
+      rope_rotate8(a, bb, cv, sv, ra, rb);
+      amax = fmaxf(amax, fmaxf(store8_half(dst + c0, ra), store8_half(dst + c0 + half, rb)));
     } else {
-      const int col = (int)(li % jb.Dp);
-      const long long rowi = li / jb.Dp;
-      const int h = (int)(rowi % jb.H);
-      const long long bs = rowi / jb.H;
-      const int s = (int)(bs % jb.S);
-      const int b = (int)(bs / jb.S);
-      const float val = stage_value<T>(jb, b, s, h, col);
-      m = fmaxf(0.f, fabsf(val));
-      jb.y[(((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.Dp + col] = __float2half_rn(val);
+      float a[8];
+      load8<T>(src + ch * 8, a);
+      amax = fmaxf(amax, store8_half(dst + ch * 8, a));
     }
-    if (j == 0) am0 = fmaxf(am0, m);
-    else if (j == 1) am1 = fmaxf(am1, m);
-    else am2 = fmaxf(am2, m);
   }
-  // Only magnitudes beyond the fp16 range matter to the fixup: other blocks
-  // skip the atomic.
-#pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    if (j >= bt.n) break;
-    const float aj = (j == 0) ? am0 : ((j == 1) ? am1 : am2);
-    const float m = block_max(aj > kHalfMax ? aj : 0.f);
-    if (threadIdx.x == 0 && m > kHalfMax) atomicMax(&bt.rec->amax_bits[bt.job[j].slot], __float_as_uint(m));
+  record_amax(bt.rec, jb.slot, amax);
+}
+
+// Staging pass, one thread per output element of the Dp-wide rows (other
+// head dims, padded with zeros; unaligned rows). Same per-block job split.
+template <typename T>
+__global__ void __launch_bounds__(256) stage_elem_kernel(const StageBatch bt) {
+  int first_block, n_blocks;
+  const int j = block_job(bt, first_block, n_blocks);
+  const StageJob jb = bt.job[j];
+  const long long total = (long long)jb.B * jb.S * jb.H * jb.Dp;
+  float amax = 0.f;
+  for (long long li = (long long)(blockIdx.x - first_block) * blockDim.x + threadIdx.x; li < total;
+       li += (long long)n_blocks * blockDim.x) {
+    const int col = (int)(li % jb.Dp);
+    const long long rowi = li / jb.Dp;
+    const int h = (int)(rowi % jb.H);
+    const long long bs = rowi / jb.H;
+    const int s = (int)(bs % jb.S);
+    const int b = (int)(bs / jb.S);
+    const float val = stage_value<T>(jb, b, s, h, col);
+    amax = fmaxf(amax, fabsf(val));
+    jb.y[(((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.Dp + col] = __float2half_rn(val);
   }
+  record_amax(bt.rec, jb.slot, amax);
 }
 
 // Exponent e >= 0 with amax * 2^-e <= 65504 (0 when amax is in range, or is
@@ -388,23 +396,36 @@ __global__ void unpad_kernel(const E* __restrict__ src, E* __restrict__ dst, int
 }
 
 template <typename T>
-cudaError_t stage_t(const StageBatch& bt, cudaStream_t st) {
+cudaError_t stage_t(const StageBatch& in, cudaStream_t st) {
+  StageBatch bt = in;
   bool vec = true;
-  long long items = 0;
+  long long items[3] = {0, 0, 0}, total = 0;
   for (int j = 0; j < bt.n; ++j) {
     const StageJob& jb = bt.job[j];
     const int need = jb.cs ? 16 : 8;
-    vec &= (jb.Dp == jb.D) && (jb.D % need == 0);
-    items += (long long)jb.B * jb.S * jb.H * jb.Dp;
+    const long long rows = (long long)jb.B * jb.S * jb.H;
+    vec &= (jb.Dp == jb.D) && (jb.D % need == 0) && (jb.D / need == 4 || jb.D / need == 8 || jb.D / need == 16) &&
+           rows * (jb.D / need) < (1ll << 31);
+    items[j] = rows * jb.Dp;
+    total += items[j];
   }
-  if (items == 0) return cudaSuccess;
+  if (total == 0) return cudaSuccess;
   const int threads = 256;
-  long long blocks = (items / (vec ? 8 : 1) + threads - 1) / threads;
-  if (blocks > 148 * 32) blocks = 148 * 32;
+  // Up to 16 blocks of 256 threads per SM, split among the jobs by size
+  // (every job with work gets at least one block).
+  long long blocks = (total / (vec ? 8 : 1) + threads - 1) / threads;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  int end = 0;
+  for (int j = 0; j < 3; ++j) {
+    int nb = 0;
+    if (j < bt.n && items[j] > 0) nb = (int)std::max<long long>(1, blocks * items[j] / total);
+    end += nb;
+    bt.blk_end[j] = end;
+  }
   if (vec)
-    stage_kernel<T, true><<<(unsigned)blocks, threads, 0, st>>>(bt);
+    stage_vec_kernel<T><<<(unsigned)end, threads, 0, st>>>(bt);
   else
-    stage_kernel<T, false><<<(unsigned)blocks, threads, 0, st>>>(bt);
+    stage_elem_kernel<T><<<(unsigned)end, threads, 0, st>>>(bt);
   note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

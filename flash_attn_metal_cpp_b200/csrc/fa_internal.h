@@ -126,6 +126,7 @@ struct StageBatch {
   int n;
   int in_dtype;
   RangeRec* rec;           // device record (zeroed before its first use)
+  int blk_end[3];          // set by launch_stage: blocks [blk_end[j-1], blk_end[j]) stage job j
 };
 
 // Stage every job of `b` (one kernel) and, in a second kernel, rescale a
