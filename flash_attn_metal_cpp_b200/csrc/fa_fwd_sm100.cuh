@@ -55,11 +55,15 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 256;  // + t * 128
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale when max grows by > 2^8
 // Of every 16 exp2 pairs, this many run as a polynomial on the FMA pipe
-// (exp2_poly2) instead of MUFU ex2. Measured on this kernel (cfg4 / cfg5a
-// kernel TFLOP/s): 0 -> 1078 / 1075, 2 -> 1063 / 1055, 4 -> 1051 / 1036,
-// 6 -> 1032 / 1010; the extra FMA-pipe instructions cost more issue slots
-// (and power, under the power cap) than the MUFU time they save.
-constexpr int kPolyPairs = 0;
+// (exp2_poly2) instead of MUFU ex2, per head dim. Measured at D = 128
+// (cfg4 / cfg5a kernel TFLOP/s): 0 -> 1078 / 1075, 2 -> 1063 / 1055,
+// 4 -> 1051 / 1036, 6 -> 1032 / 1010; the extra FMA-pipe instructions cost
+// more issue slots (and power, under the power cap) than the MUFU time they
+// save. At D = 64 a step has half the MMA work for the same exponentials,
+// and 2 of 16 pays (cfg2 / D=64 causal S8192 kernel TFLOP/s: 0 -> 376 / 635,
+// 2 -> 385 / 649, 4 -> 376 / 641, 6 -> 359 / 630).
+template <int D>
+constexpr int poly_pairs() { return D == 64 ? 2 : 0; }
 
 template <int D>
 struct Cfg {
@@ -459,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) {
             const int c = h * 64 + 2 * i;
             const float2 x = __ffma2_rn(make_float2(s[c], s[c + 1]), sc2, nm2);
-            const float2 e = ((i & 15) < kPolyPairs) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            const float2 e = ((i & 15) < poly_pairs<D>()) ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
             if (i & 1) acc1 = __fadd2_rn(acc1, e);
             else acc0 = __fadd2_rn(acc0, e);
             p[i] = pack_half2(e.x, e.y);
