@@ -577,7 +577,7 @@ def main():
     scale = scale_of(args.config, D)
     split_cfg = args.config in SPLIT_KV and world > 1  # cfg5b: rows or keys over the ranks
     split_kv = split_cfg and args.split == "kv"
-    units = None if args.config in SPLIT_KV else sharding.unit_ranges(B, Hkv, world, rank)
+    units = None if split_cfg else sharding.unit_ranges(B, Hkv, world, rank)
     if not split_cfg and units is None:
         raise SystemExit(f"{world} ranks do not split {B} x {Hkv} (batch, KV-head) units into rectangles")
     # Every rank generates the same problem (same seed) and works on its share.

@@ -149,15 +149,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const unsigned long long wlim = a.wait_limit_ns ? a.wait_limit_ns : kWaitLimitNs;
 
-  // Work item: heaviest causal blocks first, heads of one KV group adjacent.
+  // Work item. (batch, KV head) units one after another, so the CTAs in
+  // flight read the K/V tiles of one or two units and those stay in L2
+  // (an order with every unit in flight at once re-read K/V from HBM:
+  // 2.06 GB of DRAM traffic per cfg4 launch against 0.53 GB); inside a
+  // unit the heaviest causal blocks come first, the group's query heads
+  // adjacent.
   const int n_blocks = (a.q_end - a.q_begin + NT * BM - 1) / (NT * BM);
-  const int hb_count = a.Hq * a.B;
-  const int blk_rank = blockIdx.x / hb_count;
-  const int hb = blockIdx.x - blk_rank * hb_count;
-  const int hq = hb % a.Hq;
-  const int bz = hb / a.Hq;
+  const int per_unit = n_blocks * a.group;
+  const int unit = blockIdx.x / per_unit;
+  const int rem = blockIdx.x - unit * per_unit;
+  const int blk_rank = rem / a.group;
+  const int bz = unit / a.Hk;
+  const int hk = unit - bz * a.Hk;
+  const int hq = hk * a.group + (rem - blk_rank * a.group);
   const int blk = CAUSAL ? (n_blocks - 1 - blk_rank) : blk_rank;
-  const int hk = hq / a.group;
   const int q0 = a.q_begin + blk * NT * BM;
 
   // KV tiles of each query tile: absolute tiles [jlo, jhi) counted from
