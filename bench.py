@@ -744,6 +744,8 @@ def main():
     achieved = f_job * share / (kern_avg_ms / 1e3) / 1e12 if kern_launches else None
     long_region = max_ms > 1000.0
     peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
+    # DRAM bytes of one full-size attention launch (ncu launch list, committed
+    # profile), scaled to this rank's share.
     traffic = load_traffic(args.config)
     if traffic is not None:
         traffic = traffic * share
