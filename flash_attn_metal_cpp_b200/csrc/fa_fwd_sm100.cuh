@@ -38,6 +38,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
+
 namespace fa {
 namespace sm100 {
 
@@ -149,20 +151,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const unsigned long long wlim = a.wait_limit_ns ? a.wait_limit_ns : kWaitLimitNs;
 
-  // Work item. (batch, KV head) units one after another, so the CTAs in
-  // flight read the K/V tiles of one or two units and those stay in L2
-  // (an order with every unit in flight at once re-read K/V from HBM:
-  // 2.06 GB of DRAM traffic per cfg4 launch against 0.53 GB); inside a
-  // unit the heaviest causal blocks come first, the group's query heads
-  // adjacent.
+  // Work item. (batch, KV head) units are taken in groups whose K/V fit in
+  // L2 (units_per_group, chosen on the host), one group after another, so
+  // the CTAs in flight re-read K/V tiles from L2 (with every unit in flight
+  // at once a cfg4 launch moved 2.06 GB of DRAM traffic instead of 0.63 GB).
+  // Inside a group the heaviest causal blocks come first across the group's
+  // units (longest rows first keeps the launch's tail short), then the unit,
+  // then the group's query heads, adjacent.
   const int n_blocks = (a.q_end - a.q_begin + NT * BM - 1) / (NT * BM);
-  const int per_unit = n_blocks * a.group;
-  const int unit = blockIdx.x / per_unit;
-  const int rem = blockIdx.x - unit * per_unit;
-  const int blk_rank = rem / a.group;
+  const int n_units = a.B * a.Hk;
+  const int gu = a.units_per_group;
+  const int per_group = gu * n_blocks * a.group;
+  const int grp = blockIdx.x / per_group;
+  const int rem = blockIdx.x - grp * per_group;
+  const int per_rank = min(gu, n_units - grp * gu) * a.group;  // the last group may be smaller
+  const int blk_rank = rem / per_rank;
+  const int r2 = rem - blk_rank * per_rank;
+  const int unit = grp * gu + r2 / a.group;
   const int bz = unit / a.Hk;
   const int hk = unit - bz * a.Hk;
-  const int hq = hk * a.group + (rem - blk_rank * a.group);
+  const int hq = hk * a.group + (r2 - (r2 / a.group) * a.group);
   const int blk = CAUSAL ? (n_blocks - 1 - blk_rank) : blk_rank;
   const int q0 = a.q_begin + blk * NT * BM;
 
@@ -548,7 +556,13 @@ cudaError_t launch_t(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap
   if (e != cudaSuccess) return e;
   const long long blocks = (long long)((a.q_end - a.q_begin + NT * BM - 1) / (NT * BM)) * a.Hq * a.B;
   if (blocks <= 0) return cudaSuccess;
-  kern<<<dim3((unsigned)blocks), dim3(kThreads), smem, stream>>>(tq, tk, tv, a);
+  // Units per group of the CTA order: as many (batch, KV-head) units as have
+  // 32 MB of fp16 K/V together (a quarter of L2), at least one.
+  AttnArgs ag = a;
+  const long long unit_bytes = (long long)(a.kv_end - a.kv_begin) * D * 2 * 2;
+  const long long n_units = (long long)a.B * a.Hk;
+  ag.units_per_group = (int)std::max<long long>(1, std::min<long long>(n_units, (32ll << 20) / std::max(1ll, unit_bytes)));
+  kern<<<dim3((unsigned)blocks), dim3(kThreads), smem, stream>>>(tq, tk, tv, ag);
   note_launch();
   return cudaGetLastError();
 }

@@ -22,6 +22,7 @@ struct AttnArgs {
   int q_begin, q_end;      // query rows computed (partial API); [0, Sq) otherwise
   int kv_begin, kv_end;    // keys visited (split-KV); [0, Sk) otherwise
   int n_q_tiles;           // tiles of the query range for the launch
+  int units_per_group;     // CTA order: (batch, KV-head) units taken this many at a time (>= 1)
   // Direct pointers (SIMT kernel and epilogues).
   const void* q;
   const void* k;
