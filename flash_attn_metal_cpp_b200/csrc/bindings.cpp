@@ -229,6 +229,16 @@ py::object pinned_tensor(std::vector<int64_t> shape, int code) {
   return t;
 }
 
+// cos/sin table as a contiguous float32 tensor on `dev`. The staging pass
+// reads 16-byte aligned tables with vector loads and others element by
+// element, so a view that starts off a 16-byte boundary is copied.
+py::object device_table(py::module_& torch, py::object t, py::object dev) {
+  py::object x = torch.attr("as_tensor")(t, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev)
+                     .attr("contiguous")();
+  if (x.attr("data_ptr")().cast<uintptr_t>() % 16 != 0) x = x.attr("clone")();
+  return x;
+}
+
 py::object forward_torch(py::object Q, py::object K, py::object V, float scale, bool causal,
                          float dropout_p, py::object alibi, py::object window, py::object cos,
                          py::object sin, int out_code, float rope_theta, bool return_lse,
@@ -320,8 +330,8 @@ py::object forward_torch(py::object Q, py::object K, py::object V, float scale, 
   const float* cp = nullptr;
   const float* sp = nullptr;
   if (rotary_tables) {
-    ct = torch.attr("as_tensor")(cos, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
-    stt = torch.attr("as_tensor")(sin, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    ct = device_table(torch, cos, dev);
+    stt = device_table(torch, sin, dev);
     const int64_t need = std::max(qs[1], ks[1]) * (qs[3] / 2);
     if (ct.attr("numel")().cast<int64_t>() < need || stt.attr("numel")().cast<int64_t>() < need)
       forward_error("cos/sin tables must hold [max(seqlen_q, seqlen_k), head_dim/2] float32 values");
@@ -433,8 +443,8 @@ void py_forward_range(py::object Q, py::object K, py::object V, std::pair<int64_
   const float* sp = nullptr;
   if (rotary_tables) {
     py::module_ torch = py::module_::import("torch");
-    ct = torch.attr("as_tensor")(cos, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
-    stt = torch.attr("as_tensor")(sin, py::arg("dtype") = torch.attr("float32"), py::arg("device") = dev).attr("contiguous")();
+    ct = device_table(torch, cos, dev);
+    stt = device_table(torch, sin, dev);
     const int64_t need = std::max(qs[1], ks[1]) * (qs[3] / 2);
     if (ct.attr("numel")().cast<int64_t>() < need || stt.attr("numel")().cast<int64_t>() < need)
       forward_error("cos/sin tables must hold [max(seqlen_q, seqlen_k), head_dim/2] float32 values");

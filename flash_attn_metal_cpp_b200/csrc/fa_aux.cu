@@ -404,8 +404,11 @@ cudaError_t stage_t(const StageBatch& in, cudaStream_t st) {
     const StageJob& jb = bt.job[j];
     const int need = jb.cs ? 16 : 8;
     const long long rows = (long long)jb.B * jb.S * jb.H;
+    // The vector path reads table rows with 16-byte loads.
+    const bool tables16 =
+        jb.cs == nullptr || ((reinterpret_cast<uintptr_t>(jb.cs) | reinterpret_cast<uintptr_t>(jb.sn)) & 15) == 0;
     vec &= (jb.Dp == jb.D) && (jb.D % need == 0) && (jb.D / need == 4 || jb.D / need == 8 || jb.D / need == 16) &&
-           rows * (jb.D / need) < (1ll << 31);
+           rows * (jb.D / need) < (1ll << 31) && tables16;
     items[j] = rows * jb.Dp;
     total += items[j];
   }

@@ -285,6 +285,43 @@ def test_cos_sin_tables_match_theta(fa, cuda_device):
     torch.testing.assert_close(a, b, atol=2e-6, rtol=0)
 
 
+def test_unaligned_tables_through_c_abi(cuda_device):
+    """fa_forward (C ABI) with cos/sin tables 4 bytes off a 16-byte boundary:
+    the staging pass reads them element by element (its vector loads need
+    16-byte aligned table rows) and gives the aligned tables' result bit for
+    bit."""
+    import ctypes
+
+    import torch
+    from fa_ctypes import FA_BF16, FA_F32, load_lib, make_params
+
+    lib = load_lib()
+    B, S, Hq, Hk, D = 1, 640, 4, 2, 128
+    q, k, v = _inputs((B, S, Hq, D), (B, S, Hk, D), torch.bfloat16, seed=31)
+    cs, sn = orc.rope_tables(S, D, 5e5)
+    aligned = [torch.from_numpy(t).to(cuda_device) for t in (cs, sn)]
+    shifted = []
+    for t in (cs, sn):
+        base = torch.zeros(t.size + 1, device=cuda_device)
+        view = base[1:].view(t.shape)
+        view.copy_(torch.from_numpy(t))
+        assert view.data_ptr() % 16 == 4
+        shifted.append(view)
+    p = make_params(lib, B, S, S, Hq, Hk, D, True, FA_BF16, out_dtype=FA_F32)
+    p.has_rotary, p.rope_theta = 1, 0.0  # tables only
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    outs = []
+    for c, s in (aligned, shifted):
+        o = torch.empty((B, S, Hq, D), dtype=torch.float32, device=cuda_device)
+        st = lib.fa_forward(ctypes.byref(p), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), None,
+                            c.data_ptr(), s.data_ptr(), None, 0, stream)
+        assert st == 0, lib.fa_last_error()
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert lib.fa_check_device_status() == 0
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_errors_are_runtime_errors(fa, cuda_device):
     import torch
 

@@ -116,3 +116,36 @@ def test_normal_call_after_rescaled_call(fa, cuda_device):
     fa.check_status()
     assert torch.equal(a, b) and torch.equal(a, c)
     _check(a.cpu().numpy(), q, k, v, 0.088, 5e5, "ordinary call after a rescaled one")
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_q_rows_mixed_range(fa, cuda_device, D):
+    """A few query rows far beyond the fp16 range among ordinary ones (first,
+    second and ragged last query tile, several heads of a GQA group): the
+    whole staged Q takes their exponent, and the ordinary rows, scaled down
+    with it, still match the oracle. The cos/sin tables come from a view that
+    starts 4 bytes off a 16-byte boundary (the staging pass reads table rows
+    with 16-byte loads only when the tables are 16-byte aligned)."""
+    import torch
+
+    B, S, Hq, Hk, theta = 2, 777, 8, 2, 5e5
+    g = torch.Generator(device=cuda_device).manual_seed(40 + D)
+    q = torch.randn((B, S, Hq, D), generator=g, device=cuda_device)
+    k = torch.randn((B, S, Hk, D), generator=g, device=cuda_device)
+    v = torch.randn((B, S, Hk, D), generator=g, device=cuda_device)
+    for b, s, h in [(0, 0, 0), (0, 127, 3), (1, 128, 7), (1, 300, 1), (0, 776, 5)]:
+        q[b, s, h] *= 1e6
+    q, k, v = (x.to(torch.bfloat16) for x in (q, k, v))
+    cs, sn = orc.rope_tables(S, D, theta)
+    views = []
+    for t in (cs, sn):
+        base = torch.zeros(t.size + 1, device=cuda_device)
+        view = base[1:].view(t.shape)
+        view.copy_(torch.from_numpy(t))
+        assert view.data_ptr() % 16 != 0
+        views.append(view)
+    scale = 1 / math.sqrt(D)
+    out = fa.forward(q, k, v, softmax_scale=scale, is_causal=True, out_dtype="float32", cos=views[0], sin=views[1])
+    torch.cuda.synchronize()
+    fa.check_status()
+    _check(out.cpu().numpy(), q, k, v, scale, theta, f"bf16 D{D} mixed Q rows")
