@@ -131,55 +131,81 @@ __device__ __forceinline__ int block_job(const StageBatch& bt, int& first_block,
   return j;
 }
 
-// Staging pass, vectorised: each thread converts 8 consecutive columns (and,
-// with RoPE, the 8 partner columns of the other half) of one (b, s, h) row
-// with 16-byte loads and stores. Requires Dp == D, D % 16 == 0 with tables
-// (D % 8 == 0 without), 16-byte aligned rows and fewer than 2^31 chunks per
-// job (checked on the host). Each block works on one job, so the job's
-// fields sit in registers and the RoPE branch is uniform. Values are
-// written unscaled; a block whose largest magnitude exceeds the fp16 range
-// records it in rec->amax_bits (the fixup kernel then rewrites that tensor).
-template <typename T>
-__global__ void __launch_bounds__(256) stage_vec_kernel(const StageBatch bt) {
-  int first_block, n_blocks;
-  const int j = block_job(bt, first_block, n_blocks);
-  const StageJob jb = bt.job[j];
-  const bool rope = jb.cs != nullptr;
+// Items of the vectorised staging pass: one item is one 8-column chunk
+// (and, with RoPE, its partner chunk D/2 further) of G heads at one (b, s).
+// The G rows share table row s, loaded once, and their 2G 16-byte loads are
+// in flight together.
+template <typename T, int G, bool ROPE>
+__device__ __forceinline__ float stage_vec_items(const StageJob& jb, unsigned first, unsigned stride) {
   const int half = jb.D / 2;
-  const unsigned chunks = rope ? (unsigned)jb.D / 16 : (unsigned)jb.D / 8;  // 4, 8 or 16
+  const unsigned chunks = ROPE ? (unsigned)jb.D / 16 : (unsigned)jb.D / 8;  // 4, 8 or 16
   const unsigned shift = __ffs(chunks) - 1;
-  const unsigned rows = (unsigned)jb.B * jb.S * jb.H;
-  const unsigned items = rows << shift;
+  const unsigned hg = (unsigned)jb.H / G;
+  const unsigned items = ((unsigned)jb.B * jb.S * hg) << shift;
   float amax = 0.f;
-  for (unsigned li = (blockIdx.x - first_block) * blockDim.x + threadIdx.x; li < items;
-       li += (unsigned)n_blocks * blockDim.x) {
+  for (unsigned li = first; li < items; li += stride) {
     const unsigned rowi = li >> shift;
-    const int ch = (int)(li & (chunks - 1));
-    const unsigned bs = rowi / (unsigned)jb.H;
-    const int h = (int)(rowi - bs * (unsigned)jb.H);
+    const int c0 = (int)(li & (chunks - 1)) * 8;
+    const unsigned bs = rowi / hg;
+    const int h0 = (int)(rowi - bs * hg) * G;
     const unsigned b = bs / (unsigned)jb.S;
     const int s = (int)(bs - b * (unsigned)jb.S);
-    const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h * jb.sh;
-    __half* dst = jb.y + (((int64_t)b * jb.y_rows + s) * jb.H + h) * jb.D;
-    if (rope) {
-      const int c0 = ch * 8;
-      float a[8], bb[8];
-      load8<T>(src + c0, a);
-      load8<T>(src + c0 + half, bb);
+    const T* src = reinterpret_cast<const T*>(jb.x) + (int64_t)b * jb.sb + (int64_t)s * jb.ss + (int64_t)h0 * jb.sh + c0;
+    __half* dst = jb.y + (((int64_t)b * jb.y_rows + s) * jb.H + h0) * jb.D + c0;
+    if constexpr (ROPE) {
+      float a[G][8], bb[G][8];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        load8<T>(src + g * jb.sh, a[g]);
+        load8<T>(src + g * jb.sh + half, bb[g]);
+      }
       const float4* cp = reinterpret_cast<const float4*>(jb.cs + (int64_t)s * half + c0);
       const float4* sp = reinterpret_cast<const float4*>(jb.sn + (int64_t)s * half + c0);
       const float4 c_lo = cp[0], c_hi = cp[1], s_lo = sp[0], s_hi = sp[1];
       const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
       const float sv[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
-      float ra[8], rb[8];
-      rope_rotate8(a, bb, cv, sv, ra, rb);
-      amax = fmaxf(amax, fmaxf(store8_half(dst + c0, ra), store8_half(dst + c0 + half, rb)));
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float ra[8], rb[8];
+        rope_rotate8(a[g], bb[g], cv, sv, ra, rb);
+        amax = fmaxf(amax, fmaxf(store8_half(dst + g * jb.D, ra), store8_half(dst + g * jb.D + half, rb)));
+      }
     } else {
-      float a[8];
-      load8<T>(src + ch * 8, a);
-      amax = fmaxf(amax, store8_half(dst + ch * 8, a));
+      float a[G][8];
+#pragma unroll
+      for (int g = 0; g < G; ++g) load8<T>(src + g * jb.sh, a[g]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) amax = fmaxf(amax, store8_half(dst + g * jb.D, a[g]));
     }
   }
+  return amax;
+}
+
+// Staging pass, vectorised: 16-byte loads and stores, rows of up to four
+// heads at one position per item (stage_vec_items). Requires Dp == D,
+// D % 16 == 0 with tables (D % 8 == 0 without), 16-byte aligned rows and
+// fewer than 2^31 chunks per job (checked on the host). Each block works on
+// one job, so the job's fields sit in registers and the branches are
+// uniform. Values are written unscaled; a block whose largest magnitude
+// exceeds the fp16 range records it in rec->amax_bits (the fixup kernel
+// then rewrites that tensor).
+template <typename T>
+__global__ void __launch_bounds__(256) stage_vec_kernel(const StageBatch bt) {
+  grid_dep_wait();  // launched as a programmatic dependent of the previous kernel
+  grid_dep_launch_dependents();
+  int first_block, n_blocks;
+  const int j = block_job(bt, first_block, n_blocks);
+  const StageJob jb = bt.job[j];
+  const unsigned first = (blockIdx.x - first_block) * blockDim.x + threadIdx.x;
+  const unsigned stride = (unsigned)n_blocks * blockDim.x;
+  const int G = jb.H % 4 == 0 ? 4 : (jb.H % 2 == 0 ? 2 : 1);
+  float amax;
+  if (jb.cs != nullptr)
+    amax = G == 4 ? stage_vec_items<T, 4, true>(jb, first, stride)
+                  : (G == 2 ? stage_vec_items<T, 2, true>(jb, first, stride) : stage_vec_items<T, 1, true>(jb, first, stride));
+  else
+    amax = G == 4 ? stage_vec_items<T, 4, false>(jb, first, stride)
+                  : (G == 2 ? stage_vec_items<T, 2, false>(jb, first, stride) : stage_vec_items<T, 1, false>(jb, first, stride));
   record_amax(bt.rec, jb.slot, amax);
 }
 
@@ -187,6 +213,8 @@ __global__ void __launch_bounds__(256) stage_vec_kernel(const StageBatch bt) {
 // head dims, padded with zeros; unaligned rows). Same per-block job split.
 template <typename T>
 __global__ void __launch_bounds__(256) stage_elem_kernel(const StageBatch bt) {
+  grid_dep_wait();
+  grid_dep_launch_dependents();
   int first_block, n_blocks;
   const int j = block_job(bt, first_block, n_blocks);
   const StageJob jb = bt.job[j];
@@ -225,6 +253,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) stage_fixup_kernel(const StageBatch bt) {
   __shared__ int s_exp[3];
   __shared__ int s_recorded;
+  grid_dep_wait();  // the staging launch before it has finished (and its record is visible)
+  grid_dep_launch_dependents();
   RangeRec* rec = bt.rec;
   if (threadIdx.x == 0) {
     unsigned recorded = 0;
@@ -425,17 +455,14 @@ cudaError_t stage_t(const StageBatch& in, cudaStream_t st) {
     end += nb;
     bt.blk_end[j] = end;
   }
-  if (vec)
-    stage_vec_kernel<T><<<(unsigned)end, threads, 0, st>>>(bt);
-  else
-    stage_elem_kernel<T><<<(unsigned)end, threads, 0, st>>>(bt);
+  cudaError_t e = launch_pdl(vec ? stage_vec_kernel<T> : stage_elem_kernel<T>, dim3((unsigned)end), dim3(threads),
+                             0, st, bt);
   note_launch();
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // One block per SM: when nothing overflowed every block reads 16 bytes and exits.
-  stage_fixup_kernel<T><<<148, threads, 0, st>>>(bt);
+  e = launch_pdl(stage_fixup_kernel<T>, dim3(148), dim3(threads), 0, st, bt);
   note_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 }  // namespace

@@ -237,6 +237,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_addr(&bars->tmem_base), kTmemCols);
     tmem_relinquish();
   }
+  // Launched as a programmatic dependent of the staging pass (or whatever
+  // kernel ran before it on the stream): the set-up above overlaps that
+  // kernel's end; no global memory is touched before this wait.
+  grid_dep_wait();
+  grid_dep_launch_dependents();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -562,9 +567,9 @@ cudaError_t launch_t(const AttnArgs& a, const CUtensorMap& tq, const CUtensorMap
   const long long unit_bytes = (long long)(a.kv_end - a.kv_begin) * D * 2 * 2;
   const long long n_units = (long long)a.B * a.Hk;
   ag.units_per_group = (int)std::max<long long>(1, std::min<long long>(n_units, (32ll << 20) / std::max(1ll, unit_bytes)));
-  kern<<<dim3((unsigned)blocks), dim3(kThreads), smem, stream>>>(tq, tk, tv, ag);
+  e = launch_pdl(kern, dim3((unsigned)blocks), dim3(kThreads), smem, stream, tq, tk, tv, ag);
   note_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 template <int D, bool CAUSAL, bool QK_BF16>

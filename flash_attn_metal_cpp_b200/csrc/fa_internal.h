@@ -157,4 +157,22 @@ cudaError_t launch_fill_empty(const AttnArgs& a, int out_dtype, cudaStream_t str
 // Per-thread launch counter (incremented by every launch_* above).
 void note_launch();
 
+// Launch with programmatic stream serialization: the kernel may begin while
+// the previous kernel of the stream finishes; it must call grid_dep_wait()
+// (fa_ptx.cuh) in every thread before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace fa

@@ -115,6 +115,18 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Kernels launched with launch_pdl may start while the kernel before them in
+// the stream is still running. grid_dep_wait() blocks the calling thread until
+// that kernel has completed and its memory is visible; every thread calls it
+// before its first global-memory access. grid_dep_launch_dependents() lets
+// the next such kernel start launching (it still waits in grid_dep_wait).
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
