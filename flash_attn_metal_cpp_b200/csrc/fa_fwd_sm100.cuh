@@ -39,6 +39,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <type_traits>
 
 namespace fa {
 namespace sm100 {
@@ -535,7 +536,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < D; ++i) ov[i] = 0.f;
       }
-      if (row_ok) {
+      bool routed = false;
+      if constexpr (std::is_same<OutT, float>::value) routed = a.route_rows > 0;
+      if (routed) {
+        // Partial rows bound for their owner's staging slot, usually in a
+        // peer GPU's memory. One 16-byte store per thread-row would reach
+        // NVLink as 32 scattered 16-byte writes per warp instruction; instead
+        // each warp stages its 32 rows in this tile's Q buffer (free: o_full
+        // completed after the tile's last S MMA) and writes every row as a
+        // contiguous run across the warp's lanes. Two passes of D/2 columns
+        // (128 rows x D/2 fp32 = one Q tile); 16-byte chunks XOR-swizzled by
+        // row so the staging writes and reads spread over the banks.
+        constexpr int CW = D / 2;            // fp32 columns per pass
+        constexpr int CH = CW / 4;           // 16-byte chunks per staged row (16 or 8)
+        constexpr int RPI = 32 / CH;         // rows per warp store instruction
+        float* stg = reinterpret_cast<float*>(smem + C::OFF_Q + t * C::TILE_BYTES);
+        const int wrow = (warp & 3) * 32;
+        const int rows_valid = min(BM, a.q_end - (q0 + t * BM));
+        float* o_tile = reinterpret_cast<float*>(orow) - (int64_t)row * dst.o_ss;  // the tile's row 0
+#pragma unroll
+        for (int hp = 0; hp < 2; ++hp) {
+#pragma unroll
+          for (int c = 0; c < CH; ++c)
+            *reinterpret_cast<float4*>(stg + row * CW + ((c ^ (row & (CH - 1))) * 4)) =
+                make_float4(ov[hp * CW + 4 * c], ov[hp * CW + 4 * c + 1], ov[hp * CW + 4 * c + 2],
+                            ov[hp * CW + 4 * c + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 32 / RPI; ++i) {
+            const int r = wrow + i * RPI + lane / CH;
+            const int c = lane % CH;
+            if (r < rows_valid)
+              *reinterpret_cast<float4*>(o_tile + (int64_t)r * dst.o_ss + hp * CW + 4 * c) =
+                  *reinterpret_cast<const float4*>(stg + r * CW + ((c ^ (r & (CH - 1))) * 4));
+          }
+          __syncwarp();
+        }
+      } else if (row_ok) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) store_row32<OutT>(orow + c * 32, ov + c * 32);
       }
