@@ -448,7 +448,7 @@ def e2e_numpy(fa, cfg, steps=3):
 
 # ------------------------------------------------------------------ N > 1 extras
 def cfg5b_splits(fa, device, rank, world, dist, steps, warmup):
-    """cfg5b over all ranks, split by query rows (K/V replicated, no cross-rank merge)
+    """cfg5b over all ranks, split by query rows (K/V replicated, no merge)
     and by key ranges (partials stored into the row owners' staging over
     NVLink, one-element barrier, owner merge); each timed (max over ranks)
     and each rank's rows checked against an fp32 evaluation on its GPU."""
@@ -540,7 +540,7 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--split", choices=["kv", "q"], default="q",
                     help="how --config cfg5b is split over ranks: zig-zag query rows with K/V replicated (q, the "
-                         "faster: no cross-rank merge) or key ranges with partials merged by the row owners (kv)")
+                         "faster: no merge) or key ranges with partials merged by the row owners (kv)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -802,7 +802,7 @@ def main():
         if split_kv:
             parallelism = f"split-KV x{world} (key ranges {att.plan.kv_ranges}, owner rows {att.plan.owner_rows})"
         elif split_cfg:
-            parallelism = f"zig-zag query rows x{world} (K/V replicated, no cross-rank merge)"
+            parallelism = f"zig-zag query rows x{world} (K/V replicated, no merge)"
         else:
             parallelism = f"(batch, KV-head) units x{world}: {B * Hkv // world} of {B * Hkv} per rank"
         line = {

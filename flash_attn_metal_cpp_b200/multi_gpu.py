@@ -181,84 +181,34 @@ class SplitKVAttention:
 
 class QShardAttention:
     """Query-row shards with K/V replicated (the split-KV alternative that
-    needs no cross-rank merge): rank r computes row chunks r and 2W-1-r of 2W
-    against every visible key, as concurrent launches on separate streams.
+    needs no merge): rank r computes row chunks r and 2W-1-r of 2W against
+    every visible key, the two chunks as concurrent launches on two streams.
     No collective touches the data. `forward` writes the rank's rows into a
     (B, Sq, Hq, D) output (of any of the three dtypes) and leaves the other
-    rows untouched.
-
-    Under the causal mask the 256-row blocks at the end of the sequence see
-    every key, so with many ranks one such CTA can take longer than the
-    rank's average work per SM and set the rank's time (at 8 ranks on
-    S = 65536: 512 KV steps against ~443 per SM). Then the keys of the
-    heavier chunk are cut in two: both halves run as concurrent partial
-    launches (fp32 O and LSE) and a local merge (LSE-weighted, the split-KV
-    combine) writes the chunk's rows. `split_rows` is that chunk, or None."""
+    rows untouched."""
 
     def __init__(self, seqlen_q: int, rank: int, world: int, device: Optional[torch.device] = None):
         self.rank, self.world = rank, world
         self.ranges = [r for r in sharding.qshard_ranges(seqlen_q, world)[rank] if r[1] > r[0]]
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         self._side = torch.cuda.Stream(self.device)
-        self._side2 = torch.cuda.Stream(self.device)
-        self._sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self._parts = None
-        self.split_rows = None
-
-    def key_cut(self, batch: int, heads_q: int, seqlen_k: int, causal: bool) -> Optional[int]:
-        """Key index where the heavier chunk's keys are cut in two, or None
-        when its longest CTA does not exceed the rank's KV steps per SM."""
-        if not causal or not self.ranges:
-            return None
-
-        def steps(lo: int, hi: int) -> int:  # 128-key steps of the 256-row blocks of [lo, hi)
-            return sum(-(-min(seqlen_k, b + 256) // 128) for b in range(lo, hi, 256))
-
-        total = batch * heads_q * sum(steps(lo, hi) for lo, hi in self.ranges)
-        lo, hi = self.ranges[-1]
-        kv_hi = min(seqlen_k, hi)
-        if -(-kv_hi // 128) * self._sms <= total:
-            return None
-        cut = min(kv_hi // 2, lo) // 128 * 128
-        return cut if cut > 0 else None
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, softmax_scale: float, causal: bool,
                 out: torch.Tensor, cos=None, sin=None, rope_theta: Optional[float] = None, window_size=None,
                 alibi_slopes=None) -> torch.Tensor:
         main = torch.cuda.current_stream(self.device)
         kw = dict(softmax_scale=softmax_scale, is_causal=causal, cos=cos, sin=sin, rope_theta=rope_theta,
-                  window_size=window_size, alibi_slopes=alibi_slopes)
-        B, Sq, Hq, D = q.shape
+                  window_size=window_size, alibi_slopes=alibi_slopes, out_dtype=out.dtype)
         Sk = k.shape[1]
-        cut = self.key_cut(B, Hq, Sk, causal)
-        self.split_rows = self.ranges[-1] if cut is not None else None
         self._side.wait_stream(main)  # inputs written on the main stream are ready
-        if cut is not None:
-            self._side2.wait_stream(main)
         for i, (lo, hi) in enumerate(self.ranges):
             kv_hi = min(Sk, hi) if causal else Sk  # keys past the chunk's last row are masked
-            if cut is not None and i == len(self.ranges) - 1:
-                shape = (2, B, Sq, Hq, D)
-                if self._parts is None or tuple(self._parts[0].shape) != shape:
-                    self._parts = (torch.empty(shape, dtype=torch.float32, device=self.device),
-                                   torch.empty((2, B, Hq, Sq), dtype=torch.float32, device=self.device))
-                o_parts, l_parts = self._parts
-                with torch.cuda.stream(self._side):
-                    _ext.forward_range(q, k, v, (lo, hi), (0, cut), o_parts[0], l_parts[0],
-                                       out_dtype=torch.float32, **kw)
-                with torch.cuda.stream(self._side2):
-                    _ext.forward_range(q, k, v, (lo, hi), (cut, kv_hi), o_parts[1], l_parts[1],
-                                       out_dtype=torch.float32, **kw)
-            elif i == 0:
-                _ext.forward_range(q, k, v, (lo, hi), (0, kv_hi), out, out_dtype=out.dtype, **kw)
+            if i == 0:
+                _ext.forward_range(q, k, v, (lo, hi), (0, kv_hi), out, **kw)
             else:
                 with torch.cuda.stream(self._side):
-                    _ext.forward_range(q, k, v, (lo, hi), (0, kv_hi), out, out_dtype=out.dtype, **kw)
+                    _ext.forward_range(q, k, v, (lo, hi), (0, kv_hi), out, **kw)
         main.wait_stream(self._side)
-        if cut is not None:
-            main.wait_stream(self._side2)
-            o_parts, l_parts = self._parts
-            _ext.combine(o_parts, l_parts, out, q_range=self.split_rows)
         return out
 
 
